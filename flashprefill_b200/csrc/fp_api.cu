@@ -1,0 +1,481 @@
+// Host side of the C ABI declared in include/flashprefill_b200.h: argument validation,
+// workspace layout, TMA tensor maps and kernel launches.  Built as one translation unit
+// with the kernels (unity build) into libflashprefill_b200.so.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/flashprefill_b200.h"
+#include "fp_attn.cu"
+#include "fp_mean.cu"
+#include "fp_search.cu"
+
+namespace fpb {
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define FPB_CHECK_ARG(cond, ...)                       \
+  do {                                                 \
+    if (!(cond)) return fail(FPB_EINVAL, __VA_ARGS__); \
+  } while (0)
+
+#define FPB_CUDA(call)                                                                            \
+  do {                                                                                            \
+    cudaError_t e_ = (call);                                                                      \
+    if (e_ != cudaSuccess) return fail(FPB_ECUDA, "%s failed: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+#define FPB_TRY(x)                 \
+  do {                             \
+    int rc_ = (x);                 \
+    if (rc_ != FPB_OK) return rc_; \
+  } while (0)
+
+// ------------------------------------------------------------------ workspace layout
+struct Layout {
+  int64_t err, cu_tile, mk, cnt, idx, total;
+  int tiles, cap;
+};
+
+int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
+
+// varlen=0: a=batch, b=seqlen; varlen=1: a=nseq, b=total_tokens, c=max_seq_len
+Layout make_layout(int varlen, int a, int b, int c, int hq, int hk) {
+  Layout L{};
+  const int nseq = a;
+  if (!varlen) {
+    const int nb = (b + kBlock - 1) / kBlock;
+    L.tiles = a * nb;
+    L.cap = nb;
+  } else {
+    L.tiles = (b + kBlock - 1) / kBlock + a;  // sum ceil(len_i/128) <= ceil(T/128) + nseq
+    L.cap = (c + kBlock - 1) / kBlock;
+    if (L.cap < 1) L.cap = 1;
+  }
+  int64_t off = 0;
+  L.err = off;
+  off += 256;
+  L.cu_tile = off;
+  off = align256(off + 4 * (int64_t)(nseq + 1));
+  L.mk = off;
+  off = align256(off + (int64_t)L.tiles * hk * kHeadDim * 2);
+  L.cnt = off;
+  off = align256(off + 4 * (int64_t)hq * L.tiles);
+  L.idx = off;
+  off = align256(off + 4 * (int64_t)hq * L.tiles * L.cap);
+  L.total = off;
+  return L;
+}
+
+// ------------------------------------------------------------------ tensor maps
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 4-D map over (128, heads, rows, batch) 16-bit elements, box (64, 1, 128, 1), 128B swizzle.
+// Strides in elements for dims 1..3.  Size-1 dimensions get a harmless stride.
+int make_map(CUtensorMap* map, const void* base, int dtype, int64_t heads, int64_t rows, int64_t batch,
+             int64_t s_head, int64_t s_row, int64_t s_batch, const char* what) {
+  auto enc = get_encode_fn();
+  if (!enc) return fail(FPB_ECUDA, "cuTensorMapEncodeTiled is unavailable (driver too old?)");
+  if (heads == 1) s_head = 8;
+  if (batch == 1) s_batch = s_row * rows + 8;
+  const cuuint64_t dims[4] = {(cuuint64_t)kHeadDim, (cuuint64_t)heads, (cuuint64_t)rows, (cuuint64_t)batch};
+  const cuuint64_t strides[3] = {(cuuint64_t)s_head * 2, (cuuint64_t)s_row * 2, (cuuint64_t)s_batch * 2};
+  const cuuint32_t box[4] = {64, 1, 128, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dtype == FPB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FPB_ECUDA, "cuTensorMapEncodeTiled(%s) failed with CUresult %d", what, (int)r);
+  return FPB_OK;
+}
+
+// ------------------------------------------------------------------ argument checks
+int check_ptr(const void* p, const char* what) {
+  FPB_CHECK_ARG(p != nullptr, "%s is NULL", what);
+  FPB_CHECK_ARG((reinterpret_cast<uintptr_t>(p) & 15) == 0, "%s must be 16-byte aligned", what);
+  return FPB_OK;
+}
+int check_strides(const int64_t* st, int n, const char* what) {
+  FPB_CHECK_ARG(st != nullptr, "%s strides are NULL", what);
+  for (int i = 0; i < n; ++i) {
+    FPB_CHECK_ARG(st[i] >= 0 && st[i] % 8 == 0, "%s stride[%d]=%lld must be a non-negative multiple of 8 elements",
+                  what, i, (long long)st[i]);
+    FPB_CHECK_ARG(st[i] * 2 < (int64_t(1) << 40), "%s stride[%d] too large", what, i);
+  }
+  return FPB_OK;
+}
+int check_common(int dtype, int hq, int hk, int head_dim, int block_size) {
+  FPB_CHECK_ARG(dtype == FPB_BF16 || dtype == FPB_FP16, "dtype must be FPB_BF16 or FPB_FP16 (got %d)", dtype);
+  FPB_CHECK_ARG(head_dim == kHeadDim, "head_dim must be 128 (got %d)", head_dim);
+  FPB_CHECK_ARG(block_size == kBlock, "block_size must be 128 (got %d)", block_size);
+  FPB_CHECK_ARG(hq >= 1 && hk >= 1 && hq % hk == 0, "num_q_heads (%d) must be a multiple of num_kv_heads (%d)", hq,
+                hk);
+  return FPB_OK;
+}
+
+template <typename KernelT>
+int set_smem(KernelT kernel, size_t bytes) {
+  FPB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  return FPB_OK;
+}
+
+// ------------------------------------------------------------------ stage launchers
+struct Geometry {
+  int varlen, nseq, seqlen, total_tokens, max_seq_len, batch;
+  int hq, hk, dtype;
+  const int32_t* cu_seqlens;
+};
+
+SeqProblem make_problem(const Geometry& g, const Layout& L, uint8_t* ws) {
+  SeqProblem P{};
+  P.varlen = g.varlen;
+  P.nseq = g.varlen ? g.nseq : g.batch;
+  P.seqlen = g.seqlen;
+  P.nb_dense = g.varlen ? 0 : (g.seqlen + kBlock - 1) / kBlock;
+  P.tiles_ub = L.tiles;
+  P.cap = L.cap;
+  P.hq = g.hq;
+  P.hk = g.hk;
+  P.cu_seqlens = g.cu_seqlens;
+  P.cu_tile = reinterpret_cast<const int*>(ws + L.cu_tile);
+  P.err = reinterpret_cast<uint32_t*>(ws + L.err);
+  return P;
+}
+
+float score_scale() { return (float)(1.0 / std::sqrt((double)kHeadDim)) * 1.4426950408889634f; }
+
+// q/k strides as {batch, row, head} (varlen: batch stride unused)
+int run_search(const Geometry& g, const void* q, const void* k, const int64_t qs[3], const int64_t ks[3], int sink,
+               int window, float alpha, int last_n, int min_budget, int mean_model, uint8_t* ws, const Layout& L,
+               cudaStream_t stream) {
+  FPB_CHECK_ARG(mean_model == 4 || mean_model == 8, "mean_model must be 4 or 8 (got %d)", mean_model);
+  FPB_CHECK_ARG(min_budget >= 0, "min_budget must be >= 0");
+  const size_t smem = search_smem_bytes(L.cap);
+  FPB_CHECK_ARG(smem <= 227 * 1024, "sequence too long for the on-chip block search (%d blocks)", L.cap);
+  SeqProblem P = make_problem(g, L, ws);
+  FPB_CUDA(cudaMemsetAsync(ws + L.err, 0, 4, stream));
+  if (g.varlen) {
+    varlen_prep_kernel<<<1, 1024, 0, stream>>>(g.cu_seqlens, g.nseq, g.total_tokens, L.cap,
+                                               reinterpret_cast<int*>(ws + L.cu_tile), P.err);
+    FPB_CUDA(cudaGetLastError());
+  }
+  const int rows = g.varlen ? g.total_tokens : g.seqlen;
+  const int batch = g.varlen ? 1 : g.batch;
+  {
+    dim3 grid(L.tiles, g.hk);
+    if (g.dtype == FPB_BF16) {
+      auto* mk = reinterpret_cast<__nv_bfloat16*>(ws + L.mk);
+      auto* kp = reinterpret_cast<const __nv_bfloat16*>(k);
+      if (mean_model == 4) block_mean_kernel<__nv_bfloat16, 4><<<grid, 128, 0, stream>>>(kp, ks[0], ks[1], ks[2], mk, P);
+      else block_mean_kernel<__nv_bfloat16, 8><<<grid, 256, 0, stream>>>(kp, ks[0], ks[1], ks[2], mk, P);
+    } else {
+      auto* mk = reinterpret_cast<__half*>(ws + L.mk);
+      auto* kp = reinterpret_cast<const __half*>(k);
+      if (mean_model == 4) block_mean_kernel<__half, 4><<<grid, 128, 0, stream>>>(kp, ks[0], ks[1], ks[2], mk, P);
+      else block_mean_kernel<__half, 8><<<grid, 256, 0, stream>>>(kp, ks[0], ks[1], ks[2], mk, P);
+    }
+    FPB_CUDA(cudaGetLastError());
+  }
+  CUtensorMap tm_q, tm_mk;
+  FPB_TRY(make_map(&tm_q, q, g.dtype, g.hq, rows, batch, qs[2], qs[1], qs[0], "q"));
+  FPB_TRY(make_map(&tm_mk, ws + L.mk, g.dtype, g.hk, L.tiles, 1, kHeadDim, (int64_t)g.hk * kHeadDim, 0, "pooled k"));
+  SearchArgs A{};
+  A.P = P;
+  A.c = score_scale();
+  A.alpha = alpha;
+  A.cand_off = (min_budget > 0 || !(alpha > 0.f)) ? -INFINITY : std::log2(alpha) - 8.0f;
+  A.sink = sink;
+  A.window = window;
+  A.last_n = last_n;
+  A.min_budget = g.varlen ? 0 : min_budget;
+  A.normalize = g.varlen ? 0 : 1;
+  A.idx = reinterpret_cast<int32_t*>(ws + L.idx);
+  A.cnt = reinterpret_cast<int32_t*>(ws + L.cnt);
+  const unsigned grid = (unsigned)L.tiles * (unsigned)g.hq;
+  if (g.dtype == FPB_BF16) {
+    FPB_TRY(set_smem(block_search_kernel<__nv_bfloat16>, smem));
+    block_search_kernel<__nv_bfloat16><<<grid, kSearchThreads, smem, stream>>>(tm_q, tm_mk, A);
+  } else {
+    FPB_TRY(set_smem(block_search_kernel<__half>, smem));
+    block_search_kernel<__half><<<grid, kSearchThreads, smem, stream>>>(tm_q, tm_mk, A);
+  }
+  FPB_CUDA(cudaGetLastError());
+  return FPB_OK;
+}
+
+int run_attention(const Geometry& g, const void* q, const void* k, const void* v, void* o, const int64_t qs[3],
+                  const int64_t ks[3], const int64_t vs[3], const int64_t os[3], uint8_t* ws, const Layout& L,
+                  cudaStream_t stream) {
+  SeqProblem P = make_problem(g, L, ws);
+  const int rows = g.varlen ? g.total_tokens : g.seqlen;
+  const int batch = g.varlen ? 1 : g.batch;
+  CUtensorMap tm_q, tm_k, tm_v, tm_o;
+  FPB_TRY(make_map(&tm_q, q, g.dtype, g.hq, rows, batch, qs[2], qs[1], qs[0], "q"));
+  FPB_TRY(make_map(&tm_k, k, g.dtype, g.hk, rows, batch, ks[2], ks[1], ks[0], "k"));
+  FPB_TRY(make_map(&tm_v, v, g.dtype, g.hk, rows, batch, vs[2], vs[1], vs[0], "v"));
+  FPB_TRY(make_map(&tm_o, o, g.dtype, g.hq, rows, batch, os[2], os[1], os[0], "out"));
+  AttnArgs A{};
+  A.P = P;
+  A.c = score_scale();
+  A.rescale_thr = kRescaleThreshold;
+  if (const char* e = std::getenv("FLASHPREFILL_B200_RESCALE_THRESHOLD")) A.rescale_thr = (float)std::atof(e);
+  A.idx = reinterpret_cast<const int32_t*>(ws + L.idx);
+  A.cnt = reinterpret_cast<const int32_t*>(ws + L.cnt);
+  A.out = o;
+  A.o_sb = os[0];
+  A.o_ss = os[1];
+  A.o_sh = os[2];
+  const size_t smem = attn_smem_bytes();
+  const unsigned grid = (unsigned)L.tiles * (unsigned)g.hq;
+  if (g.dtype == FPB_BF16) {
+    FPB_TRY(set_smem(sparse_attn_kernel<__nv_bfloat16>, smem));
+    sparse_attn_kernel<__nv_bfloat16><<<grid, kAttnThreads, smem, stream>>>(tm_q, tm_k, tm_v, tm_o, A);
+  } else {
+    FPB_TRY(set_smem(sparse_attn_kernel<__half>, smem));
+    sparse_attn_kernel<__half><<<grid, kAttnThreads, smem, stream>>>(tm_q, tm_k, tm_v, tm_o, A);
+  }
+  FPB_CUDA(cudaGetLastError());
+  return FPB_OK;
+}
+
+int check_dense(const void* q, const void* k, int dtype, int batch, int seqlen, int hq, int hk, int head_dim,
+                const int64_t* qs, const int64_t* ks, int block_size) {
+  FPB_TRY(check_common(dtype, hq, hk, head_dim, block_size));
+  FPB_CHECK_ARG(batch >= 1 && seqlen >= 1, "batch (%d) and seqlen (%d) must be >= 1", batch, seqlen);
+  FPB_CHECK_ARG((int64_t)seqlen + kBlock < (int64_t(1) << 31), "seqlen too large");
+  FPB_TRY(check_ptr(q, "q"));
+  FPB_TRY(check_ptr(k, "k"));
+  FPB_TRY(check_strides(qs, 3, "q"));
+  FPB_TRY(check_strides(ks, 3, "k"));
+  return FPB_OK;
+}
+
+int check_dense_vo(const void* v, const void* o, const int64_t* vs, const int64_t* os) {
+  FPB_TRY(check_ptr(v, "v"));
+  FPB_TRY(check_ptr(o, "out"));
+  FPB_TRY(check_strides(vs, 3, "v"));
+  FPB_TRY(check_strides(os, 3, "out"));
+  return FPB_OK;
+}
+
+int check_varlen(const void* q, const void* k, int dtype, const int32_t* cu, int nseq, int total, int max_len, int hq,
+                 int hk, int head_dim, const int64_t* qs, const int64_t* ks, int block_size) {
+  FPB_TRY(check_common(dtype, hq, hk, head_dim, block_size));
+  FPB_CHECK_ARG(nseq >= 1, "cu_seqlens must hold at least 2 entries");
+  FPB_CHECK_ARG(total >= 0 && max_len >= 0, "total_tokens and max_seq_len must be >= 0");
+  FPB_CHECK_ARG(cu != nullptr && (reinterpret_cast<uintptr_t>(cu) & 3) == 0,
+                "cu_seqlens must be an aligned int32 pointer");
+  FPB_TRY(check_ptr(q, "q"));
+  FPB_TRY(check_ptr(k, "k"));
+  FPB_TRY(check_strides(qs, 2, "q"));
+  FPB_TRY(check_strides(ks, 2, "k"));
+  return FPB_OK;
+}
+
+int check_varlen_vo(const void* v, const void* o, const int64_t* vs, const int64_t* os) {
+  FPB_TRY(check_ptr(v, "v"));
+  FPB_TRY(check_ptr(o, "o"));
+  FPB_TRY(check_strides(vs, 2, "v"));
+  FPB_TRY(check_strides(os, 2, "o"));
+  return FPB_OK;
+}
+
+int check_ws(const void* ws, size_t bytes, const Layout& L) {
+  FPB_CHECK_ARG(ws != nullptr && (reinterpret_cast<uintptr_t>(ws) & 255) == 0,
+                "workspace must be a 256-byte aligned device pointer");
+  FPB_CHECK_ARG((int64_t)bytes >= L.total, "workspace too small: %zu bytes given, %lld needed", bytes,
+                (long long)L.total);
+  return FPB_OK;
+}
+
+void s3(const int64_t* s2, int64_t out[3]) {  // varlen {token, head} -> {batch, row, head}
+  out[0] = 0;
+  out[1] = s2[0];
+  out[2] = s2[1];
+}
+
+}  // namespace
+}  // namespace fpb
+
+using namespace fpb;
+
+extern "C" {
+
+int fpb_version(void) { return 100; }
+
+const char* fpb_last_error(void) { return g_last_error.c_str(); }
+
+size_t fpb_dense_workspace_bytes(int batch, int seqlen, int hq, int hk, int head_dim) {
+  (void)head_dim;
+  if (batch < 1 || seqlen < 1 || hq < 1 || hk < 1) return 0;
+  return (size_t)make_layout(0, batch, seqlen, 0, hq, hk).total;
+}
+
+size_t fpb_varlen_workspace_bytes(int total_tokens, int nseq, int max_seq_len, int hq, int hk, int head_dim) {
+  (void)head_dim;
+  if (nseq < 1 || total_tokens < 0 || hq < 1 || hk < 1) return 0;
+  return (size_t)make_layout(1, nseq, total_tokens, max_seq_len, hq, hk).total;
+}
+
+int fpb_workspace_layout(int varlen, int a, int b, int c, int hq, int hk, int head_dim, int64_t* out8) {
+  (void)head_dim;
+  FPB_CHECK_ARG(out8 != nullptr, "out8 is NULL");
+  FPB_CHECK_ARG(a >= 1 && b >= 0 && hq >= 1 && hk >= 1, "invalid sizes");
+  const Layout L = make_layout(varlen, a, b, c, hq, hk);
+  out8[0] = L.err;
+  out8[1] = L.cu_tile;
+  out8[2] = L.mk;
+  out8[3] = L.cnt;
+  out8[4] = L.idx;
+  out8[5] = L.total;
+  out8[6] = L.tiles;
+  out8[7] = L.cap;
+  return FPB_OK;
+}
+
+int fpb_search_dense(const void* q, const void* k, int dtype, int batch, int seqlen, int hq, int hk, int head_dim,
+                     const int64_t* q_strides, const int64_t* k_strides, int block_size, int attention_sink,
+                     int window_size, float alpha, int last_n_block_full, int min_budget, int mean_model,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  FPB_TRY(check_dense(q, k, dtype, batch, seqlen, hq, hk, head_dim, q_strides, k_strides, block_size));
+  const Layout L = make_layout(0, batch, seqlen, 0, hq, hk);
+  FPB_TRY(check_ws(workspace, workspace_bytes, L));
+  Geometry g{0, batch, seqlen, 0, 0, batch, hq, hk, dtype, nullptr};
+  return run_search(g, q, k, q_strides, k_strides, attention_sink, window_size, alpha, last_n_block_full, min_budget,
+                    mean_model, static_cast<uint8_t*>(workspace), L, static_cast<cudaStream_t>(stream));
+}
+
+int fpb_search_varlen(const void* q, const void* k, int dtype, const int32_t* cu_seqlens, int nseq, int total_tokens,
+                      int max_seq_len, int hq, int hk, int head_dim, const int64_t* q_strides,
+                      const int64_t* k_strides, int block_size, int attention_sink, int window_size, float alpha,
+                      int last_n_block, int mean_model, void* workspace, size_t workspace_bytes, void* stream) {
+  FPB_TRY(check_varlen(q, k, dtype, cu_seqlens, nseq, total_tokens, max_seq_len, hq, hk, head_dim, q_strides,
+                       k_strides, block_size));
+  const Layout L = make_layout(1, nseq, total_tokens, max_seq_len, hq, hk);
+  FPB_TRY(check_ws(workspace, workspace_bytes, L));
+  if (total_tokens == 0) return FPB_OK;
+  Geometry g{1, nseq, 0, total_tokens, max_seq_len, 1, hq, hk, dtype, cu_seqlens};
+  int64_t qs[3], ks[3];
+  s3(q_strides, qs);
+  s3(k_strides, ks);
+  return run_search(g, q, k, qs, ks, attention_sink, window_size, alpha, last_n_block, 0, mean_model,
+                    static_cast<uint8_t*>(workspace), L, static_cast<cudaStream_t>(stream));
+}
+
+int fpb_attention_dense(const void* q, const void* k, const void* v, void* out, int dtype, int batch, int seqlen,
+                        int hq, int hk, int head_dim, const int64_t* q_strides, const int64_t* k_strides,
+                        const int64_t* v_strides, const int64_t* o_strides, int block_size, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  FPB_TRY(check_dense(q, k, dtype, batch, seqlen, hq, hk, head_dim, q_strides, k_strides, block_size));
+  FPB_TRY(check_dense_vo(v, out, v_strides, o_strides));
+  const Layout L = make_layout(0, batch, seqlen, 0, hq, hk);
+  FPB_TRY(check_ws(workspace, workspace_bytes, L));
+  Geometry g{0, batch, seqlen, 0, 0, batch, hq, hk, dtype, nullptr};
+  return run_attention(g, q, k, v, out, q_strides, k_strides, v_strides, o_strides, static_cast<uint8_t*>(workspace),
+                       L, static_cast<cudaStream_t>(stream));
+}
+
+int fpb_attention_varlen(const void* q, const void* k, const void* v, void* o, int dtype, const int32_t* cu_seqlens,
+                         int nseq, int total_tokens, int max_seq_len, int hq, int hk, int head_dim,
+                         const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                         const int64_t* o_strides, int block_size, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  FPB_TRY(check_varlen(q, k, dtype, cu_seqlens, nseq, total_tokens, max_seq_len, hq, hk, head_dim, q_strides,
+                       k_strides, block_size));
+  FPB_TRY(check_varlen_vo(v, o, v_strides, o_strides));
+  const Layout L = make_layout(1, nseq, total_tokens, max_seq_len, hq, hk);
+  FPB_TRY(check_ws(workspace, workspace_bytes, L));
+  if (total_tokens == 0) return FPB_OK;
+  Geometry g{1, nseq, 0, total_tokens, max_seq_len, 1, hq, hk, dtype, cu_seqlens};
+  int64_t qs[3], ks[3], vs[3], os[3];
+  s3(q_strides, qs);
+  s3(k_strides, ks);
+  s3(v_strides, vs);
+  s3(o_strides, os);
+  return run_attention(g, q, k, v, o, qs, ks, vs, os, static_cast<uint8_t*>(workspace), L,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int fpb_prefill_dense(const void* q, const void* k, const void* v, void* out, int dtype, int batch, int seqlen,
+                      int hq, int hk, int head_dim, const int64_t* q_strides, const int64_t* k_strides,
+                      const int64_t* v_strides, const int64_t* o_strides, int block_size, int attention_sink,
+                      int window_size, float alpha, int last_n_block_full, int min_budget, int mean_model,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  FPB_TRY(check_dense(q, k, dtype, batch, seqlen, hq, hk, head_dim, q_strides, k_strides, block_size));
+  FPB_TRY(check_dense_vo(v, out, v_strides, o_strides));
+  const Layout L = make_layout(0, batch, seqlen, 0, hq, hk);
+  FPB_TRY(check_ws(workspace, workspace_bytes, L));
+  Geometry g{0, batch, seqlen, 0, 0, batch, hq, hk, dtype, nullptr};
+  auto* ws = static_cast<uint8_t*>(workspace);
+  auto st = static_cast<cudaStream_t>(stream);
+  FPB_TRY(run_search(g, q, k, q_strides, k_strides, attention_sink, window_size, alpha, last_n_block_full, min_budget,
+                     mean_model, ws, L, st));
+  return run_attention(g, q, k, v, out, q_strides, k_strides, v_strides, o_strides, ws, L, st);
+}
+
+int fpb_prefill_varlen(const void* q, const void* k, const void* v, void* o, int dtype, const int32_t* cu_seqlens,
+                       int nseq, int total_tokens, int max_seq_len, int hq, int hk, int head_dim,
+                       const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                       const int64_t* o_strides, int block_size, int attention_sink, int window_size, float alpha,
+                       int last_n_block, int mean_model, void* workspace, size_t workspace_bytes, void* stream) {
+  FPB_TRY(check_varlen(q, k, dtype, cu_seqlens, nseq, total_tokens, max_seq_len, hq, hk, head_dim, q_strides,
+                       k_strides, block_size));
+  FPB_TRY(check_varlen_vo(v, o, v_strides, o_strides));
+  const Layout L = make_layout(1, nseq, total_tokens, max_seq_len, hq, hk);
+  FPB_TRY(check_ws(workspace, workspace_bytes, L));
+  if (total_tokens == 0) return FPB_OK;
+  Geometry g{1, nseq, 0, total_tokens, max_seq_len, 1, hq, hk, dtype, cu_seqlens};
+  int64_t qs[3], ks[3], vs[3], os[3];
+  s3(q_strides, qs);
+  s3(k_strides, ks);
+  s3(v_strides, vs);
+  s3(o_strides, os);
+  auto* ws = static_cast<uint8_t*>(workspace);
+  auto st = static_cast<cudaStream_t>(stream);
+  FPB_TRY(run_search(g, q, k, qs, ks, attention_sink, window_size, alpha, last_n_block, 0, mean_model, ws, L, st));
+  return run_attention(g, q, k, v, o, qs, ks, vs, os, ws, L, st);
+}
+
+int fpb_read_device_error(const void* workspace, uint32_t* flags, void* stream) {
+  FPB_CHECK_ARG(workspace != nullptr && flags != nullptr, "NULL argument");
+  auto st = static_cast<cudaStream_t>(stream);
+  uint32_t h = 0;
+  FPB_CUDA(cudaMemcpyAsync(&h, workspace, 4, cudaMemcpyDeviceToHost, st));
+  FPB_CUDA(cudaStreamSynchronize(st));
+  *flags = h;
+  if (h) return fail(FPB_EDEVICE, "device error bits 0x%x", h);
+  return FPB_OK;
+}
+
+}  // extern "C"

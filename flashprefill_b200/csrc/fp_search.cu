@@ -1,0 +1,354 @@
+// Fused block search: pooled-key scores, per-block max / exp-sum, normalisation,
+// threshold + structural rules, and compaction into an ascending int32 block list --
+// one CTA per (query block, query head), nothing but the list and its count written.
+//
+// Reference semantics (paths relative to the reference project):
+//   scores   ops/flashprefill_native_forward.py:129-188, ops/flashprefill_varlen_func.py:158-217
+//            s[r,kb] = c * (q_r . mk_kb), c = fp32(1/sqrt(D)) * fp32(log2 e); row r of query
+//            block qb is causal for kb iff qb*128 + r >= kb*128 + 127 (so the diagonal block
+//            sees only row 127, and zero-padded rows past the sequence end count as s = 0);
+//            m[kb] = max_r s, p[kb] = sum_r exp2(s - m).
+//   normalise native:388-403 (dense: pw / (sum pw + 1e-9)), varlen:240-304,656 (pw only),
+//            pw[kb] = p[kb] * exp2(m[kb] - max_kb m).
+//   select   native:347-385, varlen:327-409: score >= alpha * max score, or kb < sink, or
+//            0 <= qb - kb < window, or qb >= nb - last_n; AND kb <= qb.  Dense min_budget > 0
+//            also forces the top-min_budget scores in (ties: lower block index first).
+//   output   ascending block indices (what the reference's sort / boolean compaction yields,
+//            native:379-383, varlen:683-698) and the per-row count.
+//
+// The reference materialises (NB, NB, Hq) fp32 score and max tensors and sorts an int64
+// copy; here everything after the MMA stays on chip.  Roles (192 threads): warp 0 issues
+// TMA loads (query block once, pooled-key tiles of 128 blocks into a 2-stage ring), warp 1
+// issues tcgen05.mma D[kb, r] = mk_kb . q_r into a double-buffered 128x128 fp32 TMEM
+// accumulator, warps 2-5 read one TMEM lane (= one key block) each and reduce its 128
+// query rows.
+//
+// exp2 work is skipped where it cannot change the result: with M = max_kb m, every
+// block's pw <= 128 * 2^(m - M) while the best block has pw >= 1, so a block with
+// m < M + log2(alpha) - 8 scores below alpha/2 of the maximum and cannot pass the
+// threshold.  A running lower bound of M is used while scanning, which only widens the
+// set of evaluated blocks.  (With min_budget > 0 every causal block is evaluated.)
+#include "fp_common.cuh"
+
+namespace fpb {
+
+struct SearchArgs {
+  SeqProblem P;
+  float c;          // score scale in log2 units
+  float alpha;
+  float cand_off;   // log2(alpha) - 8, or -inf to evaluate every block
+  int sink, window, last_n, min_budget;
+  int normalize;    // dense path: divide by (sum + 1e-9)
+  int32_t* idx;     // [hq][tiles_ub][cap]
+  int32_t* cnt;     // [hq][tiles_ub]
+};
+
+constexpr int kSearchThreads = 192;
+constexpr uint32_t kTileBytes = 128 * 128 * 2;  // one 128x128 16-bit tile (two 64-column TMA boxes)
+constexpr uint32_t kHalfTile = kTileBytes / 2;
+
+__host__ __device__ constexpr size_t search_smem_bytes(int cap) {
+  // Q + 2 pooled-key stages + m/p arrays + top-k marks + barriers/scalars + alignment slack
+  return 3 * (size_t)kTileBytes + 8 * (size_t)cap + (size_t)((cap + 31) / 32) * 4 + 256 + 1024;
+}
+
+// Sum / max over the 128 epilogue threads (warps 2..5); uses named barrier 1.
+__device__ __forceinline__ float epi_reduce_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int wq = (threadIdx.x >> 5) - 2;
+  named_bar_sync(1, 128);
+  if ((threadIdx.x & 31) == 0) red[wq] = v;
+  named_bar_sync(1, 128);
+  return (red[0] + red[1]) + (red[2] + red[3]);
+}
+__device__ __forceinline__ float epi_reduce_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int wq = (threadIdx.x >> 5) - 2;
+  named_bar_sync(1, 128);
+  if ((threadIdx.x & 31) == 0) red[wq] = v;
+  named_bar_sync(1, 128);
+  return fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kSearchThreads, 1)
+    block_search_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_mk,
+                        const SearchArgs A) {
+  const int hq = blockIdx.x % A.P.hq;
+  SeqInfo s;
+  int qb;
+  if (!decode_item(A.P, blockIdx.x / A.P.hq, s, qb)) return;
+  const int hk = hq / (A.P.hq / A.P.hk);
+  const int row = s.tile_base + qb;
+  int32_t* out_idx = A.idx + ((int64_t)hq * A.P.tiles_ub + row) * A.P.cap;
+  int32_t* out_cnt = A.cnt + (int64_t)hq * A.P.tiles_ub + row;
+
+  // Rows in the last-N band, or alpha <= 0: every causal block is selected.
+  if (qb >= s.nb - A.last_n || A.alpha <= 0.f) {
+    for (int kb = threadIdx.x; kb <= qb; kb += blockDim.x) out_idx[kb] = kb;
+    if (threadIdx.x == 0) *out_cnt = qb + 1;
+    return;
+  }
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sMK = smem + kTileBytes;  // 2 stages
+  float* m_arr = reinterpret_cast<float*>(smem + 3 * kTileBytes);
+  float* p_arr = m_arr + A.P.cap;
+  uint32_t* marks = reinterpret_cast<uint32_t*>(p_arr + A.P.cap);
+  uint8_t* tail = reinterpret_cast<uint8_t*>(marks + (A.P.cap + 31) / 32);
+  tail = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tail) + 15) & ~uintptr_t(15));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(tail);
+  uint64_t* q_full = bars + 0;
+  uint64_t* mk_full = bars + 1;    // [2]
+  uint64_t* mk_empty = bars + 3;   // [2]
+  uint64_t* acc_full = bars + 5;   // [2]
+  uint64_t* acc_empty = bars + 7;  // [2]
+  uint64_t* mma_done = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* mrun = reinterpret_cast<int*>(tmem_slot + 2);
+  float* red = reinterpret_cast<float*>(tmem_slot + 4);   // 4 floats
+  int* red_i = reinterpret_cast<int*>(tmem_slot + 8);     // 4 ints
+  int* red_k = reinterpret_cast<int*>(tmem_slot + 12);    // 4 ints
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ntiles = qb / kBlock + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(mk_full + i, 1);
+      mbar_init(mk_empty + i, 1);
+      mbar_init(acc_full + i, 1);
+      mbar_init(acc_empty + i, 128);
+    }
+    mbar_init(mma_done, 1);
+    *abort = 0;
+    *mrun = float_to_ordered(-INFINITY);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_q);
+      prefetch_tmap(&tm_mk);
+      const int qrow = s.start + qb * kBlock;
+      mbar_arrive_expect_tx(q_full, kTileBytes);
+      tma_load_4d(sQ, &tm_q, q_full, 0, hq, qrow, s.bcoord);
+      tma_load_4d(sQ + kHalfTile, &tm_q, q_full, 64, hq, qrow, s.bcoord);
+      int issued = 0;
+      for (int t = 0; t < ntiles; ++t) {
+        const int st = t & 1;
+        if (!mbar_wait(mk_empty + st, ((t >> 1) & 1) ^ 1, abort)) break;
+        mbar_arrive_expect_tx(mk_full + st, kTileBytes);
+        uint8_t* dst = sMK + st * kTileBytes;
+        const int mrow = s.tile_base + t * kBlock;
+        tma_load_4d(dst, &tm_mk, mk_full + st, 0, hk, mrow, 0);
+        tma_load_4d(dst + kHalfTile, &tm_mk, mk_full + st, 64, hk, mrow, 0);
+        issued = t + 1;
+      }
+      if (*abort) {  // let loads still in flight land before the CTA exits
+        volatile int no_abort = 0;
+        for (int t = (issued > 2 ? issued - 2 : 0); t < issued; ++t)
+          mbar_wait(mk_full + (t & 1), (t >> 1) & 1, &no_abort);
+        mbar_wait(q_full, 0, &no_abort);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(128, 128, DT<T>::is_bf16, false);
+      const uint32_t q_base = smem_u32(sQ);
+      if (mbar_wait(q_full, 0, abort)) {
+        for (int t = 0; t < ntiles; ++t) {
+          const int st = t & 1, acc = t & 1;
+          if (!mbar_wait(mk_full + st, (t >> 1) & 1, abort)) break;
+          if (!mbar_wait(acc_empty + acc, ((t >> 1) & 1) ^ 1, abort)) break;
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sMK + st * kTileBytes);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t off = (ks >> 2) * kHalfTile + (ks & 3) * 32;
+            umma_ss(tmem + acc * 128, sdesc_sw128(a_base + off, 16, 1024), sdesc_sw128(q_base + off, 16, 1024),
+                    idesc, ks > 0);
+          }
+          umma_commit(mk_empty + st);
+          umma_commit(acc_full + acc);
+        }
+      }
+      umma_commit(mma_done);
+      volatile int no_abort = 0;
+      mbar_wait(mma_done, 0, &no_abort);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    const int quad = warp & 3;
+    const int et = threadIdx.x - 64;       // 0..127 within the epilogue group
+    const int lrow = quad * 32 + lane;     // TMEM lane = key block within the tile
+    const int vr = min(kBlock, s.len - qb * kBlock);  // valid query rows of this block
+    const float c = A.c;
+    bool ok = true;
+    for (int t = 0; t < ntiles; ++t) {
+      const int acc = t & 1;
+      if (!mbar_wait_warp(acc_full + acc, (t >> 1) & 1, abort)) { ok = false; break; }
+      tc_fence_after();
+      const int kb = t * kBlock + lrow;
+      const uint32_t taddr = tmem + acc * 128 + ((uint32_t)(quad * 32) << 16);
+      float mx = -INFINITY, s127 = 0.f;
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t r[32];
+        tmem_ld32(taddr + ch * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float v = __uint_as_float(r[i]);
+          if (ch * 32 + i < vr) mx = fmaxf(mx, v);
+        }
+        if (ch == 3) s127 = __uint_as_float(r[31]);
+      }
+      if (vr < kBlock) {
+        mx = fmaxf(mx, 0.f);   // padded rows: q = 0
+        s127 = 0.f;
+      }
+      const bool causal = kb <= qb;
+      const bool diag = kb == qb;
+      float m = -INFINITY;
+      if (causal) m = __fmul_rn(diag ? s127 : mx, c);
+      // running lower bound of the row maximum
+      float wm = m;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, o));
+      const float m_est = fmaxf(wm, ordered_to_float(*(volatile int*)mrun));
+      if (lane == 0 && wm > -INFINITY) atomicMax(mrun, float_to_ordered(wm));
+      const bool cand = causal && (m >= m_est + A.cand_off);
+      float p = 0.f;
+      if (__any_sync(0xffffffffu, cand && !diag)) {
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t r[32];
+          tmem_ld32(taddr + ch * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float sv = __fmul_rn(__uint_as_float(r[i]), c);
+            const float e = ex2_approx(__fsub_rn(sv, m));
+            if (ch * 32 + i < vr) p += e;
+          }
+        }
+        if (vr < kBlock) p += (float)(kBlock - vr) * ex2_approx(-m);
+      }
+      if (diag) p = 1.f;
+      tc_fence_before();
+      mbar_arrive(acc_empty + acc);
+      if (causal) {
+        m_arr[kb] = m;
+        p_arr[kb] = cand ? p : -1.f;
+      }
+    }
+    // ---- normalise, threshold, compact
+    named_bar_sync(1, 128);
+    const bool failed = __any_sync(0xffffffffu, !ok || *abort);
+    if (failed) {
+      if (et == 0) *out_cnt = 0;
+    } else {
+      const float M = ordered_to_float(*(volatile int*)mrun);
+      float part = 0.f;
+      for (int kb = et; kb <= qb; kb += 128) {
+        const float pv = p_arr[kb];
+        const float pw = pv >= 0.f ? __fmul_rn(pv, ex2_approx(__fsub_rn(m_arr[kb], M))) : -1.f;
+        p_arr[kb] = pw;
+        if (pw > 0.f) part += pw;
+      }
+      const float denom = A.normalize ? __fadd_rn(epi_reduce_sum(part, red), 1e-9f) : 1.f;
+      float best = 0.f;
+      for (int kb = et; kb <= qb; kb += 128) {
+        const float pw = p_arr[kb];
+        if (pw >= 0.f) {
+          const float sc = A.normalize ? __fdiv_rn(pw, denom) : pw;
+          p_arr[kb] = sc;
+          best = fmaxf(best, sc);
+        }
+      }
+      const float top1 = epi_reduce_max(best, red);
+      const float thr = __fmul_rn(top1, A.alpha);
+      // dense min_budget: force the top-k scores in (ties -> lower block index)
+      const int nwords = (qb + 1 + 31) / 32;
+      for (int wd = et; wd < nwords; wd += 128) marks[wd] = 0u;
+      named_bar_sync(1, 128);
+      const int kbudget = min(A.min_budget, qb + 1);
+      for (int it = 0; it < kbudget; ++it) {
+        float bv = -INFINITY;
+        int bk = 0x7fffffff;
+        for (int kb = et; kb <= qb; kb += 128) {
+          if (marks[kb >> 5] & (1u << (kb & 31))) continue;
+          const float v = fmaxf(p_arr[kb], 0.f);
+          if (v > bv || (v == bv && kb < bk)) { bv = v; bk = kb; }
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int ok2 = __shfl_xor_sync(0xffffffffu, bk, o);
+          if (ov > bv || (ov == bv && ok2 < bk)) { bv = ov; bk = ok2; }
+        }
+        const int wq = warp - 2;
+        if (lane == 0) { red[wq] = bv; red_k[wq] = bk; }
+        named_bar_sync(1, 128);
+        if (et == 0) {
+          float v0 = red[0];
+          int k0 = red_k[0];
+          for (int j = 1; j < 4; ++j)
+            if (red[j] > v0 || (red[j] == v0 && red_k[j] < k0)) { v0 = red[j]; k0 = red_k[j]; }
+          if (k0 <= qb) marks[k0 >> 5] |= 1u << (k0 & 31);
+        }
+        named_bar_sync(1, 128);
+      }
+      // selection + ascending compaction, 128 blocks per round
+      int base = 0;
+      for (int k0 = 0; k0 <= qb; k0 += 128) {
+        const int kb = k0 + et;
+        bool sel = false;
+        if (kb <= qb) {
+          const float sc = p_arr[kb];
+          const bool by_score = sc >= 0.f ? (sc >= thr) : (0.f >= thr);
+          const bool forced = (marks[kb >> 5] >> (kb & 31)) & 1u;
+          sel = by_score || forced || kb < A.sink || (qb - kb) < A.window;
+        }
+        const uint32_t bal = __ballot_sync(0xffffffffu, sel);
+        const int wq = warp - 2;
+        named_bar_sync(1, 128);
+        if (lane == 0) red_i[wq] = __popc(bal);
+        named_bar_sync(1, 128);
+        int pre = base;
+        for (int j = 0; j < wq; ++j) pre += red_i[j];
+        pre += __popc(bal & ((1u << lane) - 1u));
+        if (sel) out_idx[pre] = kb;
+        base += red_i[0] + red_i[1] + red_i[2] + red_i[3];
+      }
+      if (et == 0) *out_cnt = base;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+  if (threadIdx.x == 0 && *abort) raise_error(A.P.err, kErrWaitTimeout);
+}
+
+}  // namespace fpb

@@ -1,0 +1,144 @@
+/* flashprefill_b200 -- C ABI of the B200 (sm_100a) sparse-prefill operator.
+ *
+ * The library replaces the device work behind the two public entry points of
+ * FlashPrefill (qhfan/FlashPrefill, paths relative to that project):
+ *   ops/flashprefill_native_forward.py:481-499  flash_prefill(q, k, v, out, block_size,
+ *       attention_sink, window_size, alpha, last_n_block_full, min_budget)
+ *   ops/flashprefill_varlen_func.py:723-743     flash_prefill_varlen_func(q, k, v, o,
+ *       cu_seqlens, max_seq_len, alpha, block_size, attention_sink, window_size, last_n_block)
+ * Those Python functions launch Triton kernels; here the same work is three CUDA kernels
+ * (pooled keys, fused block search, tcgen05 block-sparse attention).  All pointers are
+ * device pointers unless stated; all calls are asynchronous on `stream` (a cudaStream_t,
+ * NULL = legacy default stream) and never synchronise the host, except
+ * fpb_read_device_error.  Return value: FPB_OK or an FPB_E* code; fpb_last_error()
+ * describes the most recent failure of the calling thread.
+ *
+ * Tensor layout: dense q/k/v/out are (batch, seq, heads, 128) with the last dimension
+ * contiguous and strides given in ELEMENTS as {batch, seq, head}; varlen tensors are
+ * (tokens, heads, 128) with strides {token, head}.  Strides must be multiples of 8
+ * elements (16 bytes) and base pointers 16-byte aligned.  dtype: FPB_BF16 or FPB_FP16;
+ * q, k, v and out share it.  head_dim and block_size must be 128.
+ *
+ * Workspace: the caller provides `workspace` of at least the size returned by the
+ * matching *_workspace_bytes function (the reference allocates its temporaries from the
+ * PyTorch caching allocator, native:419-434 / varlen:596-663; here they are one caller
+ * buffer).  It holds the device error word, cu_tile, the pooled keys, and the per-head
+ * block lists.  Its layout is reported by fpb_workspace_layout.
+ */
+#ifndef FLASHPREFILL_B200_H
+#define FLASHPREFILL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FPB_API __attribute__((visibility("default")))
+#else
+#define FPB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FPB_OK 0
+#define FPB_EINVAL 1   /* invalid argument (shape, dtype, stride, alignment, size) */
+#define FPB_ECUDA 2    /* a CUDA runtime/driver call or a kernel launch failed */
+#define FPB_EDEVICE 3  /* fpb_read_device_error found error bits set */
+
+#define FPB_BF16 0
+#define FPB_FP16 1
+
+/* Device error bits (fpb_read_device_error). */
+#define FPB_DEV_WAIT_TIMEOUT 1u   /* a pipeline wait ran out of time; the kernel bailed out */
+#define FPB_DEV_BAD_SEQLENS 2u    /* cu_seqlens not non-decreasing from 0 to total_tokens */
+#define FPB_DEV_SEQ_TOO_LONG 4u   /* a sequence longer than max_seq_len (rows skipped) */
+#define FPB_DEV_INDEX_RANGE 8u    /* a block list held an index outside [0, query block] */
+
+/* Library version (major*10000 + minor*100 + patch). */
+FPB_API int fpb_version(void);
+
+/* Message for the last failing call on this thread ("" if none). */
+FPB_API const char* fpb_last_error(void);
+
+/* Workspace size for the dense entry points (replaces the temporaries of
+ * ops/flashprefill_native_forward.py:419-434 and deal_output_score's outputs :379-385). */
+FPB_API size_t fpb_dense_workspace_bytes(int batch, int seqlen, int hq, int hk, int head_dim);
+
+/* Workspace size for the varlen entry points (replaces
+ * ops/flashprefill_varlen_func.py:596-698).  Sized from host-known bounds only, so no
+ * device->host copy of cu_seqlens is needed. */
+FPB_API size_t fpb_varlen_workspace_bytes(int total_tokens, int nseq, int max_seq_len, int hq, int hk,
+                                          int head_dim);
+
+/* Byte offsets inside the workspace.  out[8] = {error word, cu_tile (int32[nseq+1]),
+ * pooled keys (dtype[tiles][hk][128]), counts (int32[hq][tiles]), block lists
+ * (int32[hq][tiles][cap]), total bytes, tiles, cap}.  Row `tile_base(seq)+qb` of head h:
+ * counts[h*tiles + row] entries at lists[(h*tiles + row)*cap ...], ascending.
+ * varlen = 0: a = batch, b = seqlen, c ignored.  varlen = 1: a = nseq, b = total_tokens,
+ * c = max_seq_len.  (The reference keeps the same information as block_index/counts,
+ * native:377-385, or out_index/out_number_cu, varlen:683-698.) */
+FPB_API int fpb_workspace_layout(int varlen, int a, int b, int c, int hq, int hk, int head_dim, int64_t* out8);
+
+/* Whole operator, dense layout: replaces FlashPrefill.forward
+ * (ops/flashprefill_native_forward.py:405-476).  Writes out in place.
+ * mean_model: 4 or 8, the warp count whose reduction order the pooled-key sum follows
+ * (the reference autotunes it, native:7-20). */
+FPB_API int fpb_prefill_dense(const void* q, const void* k, const void* v, void* out, int dtype, int batch,
+                              int seqlen, int hq, int hk, int head_dim, const int64_t* q_strides,
+                              const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                              int block_size, int attention_sink, int window_size, float alpha,
+                              int last_n_block_full, int min_budget, int mean_model, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
+/* Whole operator, packed varlen layout: replaces FlashPrefill_varlen.forward
+ * (ops/flashprefill_varlen_func.py:577-720).  cu_seqlens: device int32[nseq+1]. */
+FPB_API int fpb_prefill_varlen(const void* q, const void* k, const void* v, void* o, int dtype,
+                               const int32_t* cu_seqlens, int nseq, int total_tokens, int max_seq_len, int hq,
+                               int hk, int head_dim, const int64_t* q_strides, const int64_t* k_strides,
+                               const int64_t* v_strides, const int64_t* o_strides, int block_size,
+                               int attention_sink, int window_size, float alpha, int last_n_block, int mean_model,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* Search stage only (pooled keys + block lists into the workspace): replaces
+ * compute_mean_vector + compute_block_score + normalize_scores + deal_output_score
+ * (ops/flashprefill_native_forward.py:22-188,347-403). */
+FPB_API int fpb_search_dense(const void* q, const void* k, int dtype, int batch, int seqlen, int hq, int hk,
+                             int head_dim, const int64_t* q_strides, const int64_t* k_strides, int block_size,
+                             int attention_sink, int window_size, float alpha, int last_n_block_full,
+                             int min_budget, int mean_model, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Search stage only, varlen: replaces ops/flashprefill_varlen_func.py:8-18,35-409,656-698. */
+FPB_API int fpb_search_varlen(const void* q, const void* k, int dtype, const int32_t* cu_seqlens, int nseq,
+                              int total_tokens, int max_seq_len, int hq, int hk, int head_dim,
+                              const int64_t* q_strides, const int64_t* k_strides, int block_size,
+                              int attention_sink, int window_size, float alpha, int last_n_block, int mean_model,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* Attention stage only, over the block lists already in the workspace (written by
+ * fpb_search_* or by the caller): replaces _flash_forward
+ * (ops/flashprefill_native_forward.py:228-344). */
+FPB_API int fpb_attention_dense(const void* q, const void* k, const void* v, void* out, int dtype, int batch,
+                                int seqlen, int hq, int hk, int head_dim, const int64_t* q_strides,
+                                const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                                int block_size, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Attention stage only, varlen: replaces _flash_block_sparse_varlen
+ * (ops/flashprefill_varlen_func.py:449-575).  Needs cu_tile in the workspace, which
+ * fpb_search_varlen writes. */
+FPB_API int fpb_attention_varlen(const void* q, const void* k, const void* v, void* o, int dtype,
+                                 const int32_t* cu_seqlens, int nseq, int total_tokens, int max_seq_len, int hq,
+                                 int hk, int head_dim, const int64_t* q_strides, const int64_t* k_strides,
+                                 const int64_t* v_strides, const int64_t* o_strides, int block_size,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* Synchronises `stream`, copies the device error word of `workspace` to *flags and
+ * returns FPB_EDEVICE if any bit is set.  No counterpart in the reference, which has no
+ * device-side error reporting. */
+FPB_API int fpb_read_device_error(const void* workspace, uint32_t* flags, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASHPREFILL_B200_H */

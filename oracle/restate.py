@@ -7,14 +7,14 @@ timed CPU baseline.  The product path (``flashprefill_b200``) never calls it.
 Every stage restates one piece of the reference (paths relative to the reference
 project root):
 
-* ``block_mean``      -- ops/flashprefill_native_forward.py:22-67 (compute_mean_vector),
-                         ops/flashprefill_varlen_func.py:35-85 (compute_mean_vector_varlen)
-* ``block_scores``    -- ops/flashprefill_native_forward.py:88-188 (compute_block_score),
-                         ops/flashprefill_varlen_func.py:107-217
-* ``select_blocks``   -- ops/flashprefill_native_forward.py:347-403 (deal_output_score,
-                         normalize_scores); ops/flashprefill_varlen_func.py:240-409,656
-* ``sparse_attention``-- ops/flashprefill_native_forward.py:228-344 (_flash_forward),
-                         ops/flashprefill_varlen_func.py:449-575
+* ``block_mean``        -- ops/flashprefill_native_forward.py:22-67 (compute_mean_vector),
+                           ops/flashprefill_varlen_func.py:35-85 (compute_mean_vector_varlen)
+* ``block_scores_head`` -- ops/flashprefill_native_forward.py:88-188 (compute_block_score),
+                           ops/flashprefill_varlen_func.py:107-217
+* ``select_row``        -- ops/flashprefill_native_forward.py:347-403 (deal_output_score,
+                           normalize_scores); ops/flashprefill_varlen_func.py:240-409,656
+* ``sparse_attention``  -- ops/flashprefill_native_forward.py:228-344 (_flash_forward),
+                           ops/flashprefill_varlen_func.py:449-575
 
 Values of 16-bit dtypes are carried as float32 arrays that hold exactly representable
 values; ``round_to`` performs the round-to-nearest-even conversion.
@@ -27,9 +27,10 @@ Pooled-K rounding models (the only place where summation order changes selected 
 * ``"tw4"``/``"tw8"``  the order Triton's reduction uses on the GPU for a 128x128 16-bit
                tile with 4 / 8 warps: each thread sums its rows sequentially (row = rep*2W
                + 2w + l), the lane pair (l=0,1) is combined, then the W warp partials are
-               combined pairwise (butterfly).  Every add rounds to the input dtype.  Which
-               of the two the reference picks depends on its autotuner, so it is a
-               parameter here and in the CUDA kernel (default ``"tw4"``).
+               combined by xor shuffles of distance W/2, ..., 1 (W=4: (w0+w2)+(w1+w3)).
+               Every add rounds to the input dtype.  Which of the two the reference picks
+               depends on its autotuner, so it is a parameter here and in the CUDA kernel
+               (default ``"tw4"``).
 """
 from __future__ import annotations
 
@@ -70,7 +71,7 @@ def scale_log2(head_dim: int) -> np.float32:
 
 # ---------------------------------------------------------------------- sequences
 def seq_layout(cu_seqlens, block: int = 128):
-    """Per-sequence (start, length, nb, tile_base) and cu_tile -- varlen:8-18."""
+    """Per-sequence (start, length, nb, tile_base) and the total block count -- varlen:8-18."""
     cu = [int(x) for x in cu_seqlens]
     out, base = [], 0
     for i in range(len(cu) - 1):
@@ -82,14 +83,12 @@ def seq_layout(cu_seqlens, block: int = 128):
 
 
 # ------------------------------------------------------------------- pooled keys
-def _mean_tile(x: np.ndarray, n_valid: int, dt: str, model: str) -> np.ndarray:
-    """Mean of one (128, D) tile whose rows >= n_valid are zero -- native:47-58."""
-    if n_valid <= 0:
-        return np.zeros(x.shape[1], np.float32)
+def _mean_tiles(x: np.ndarray, n_valid: np.ndarray, dt: str, model: str) -> np.ndarray:
+    """Means of tiles x (nt, 128, ...) whose rows >= n_valid[t] are zero -- native:47-58."""
     if model == "seq32":
-        acc = x[0].astype(np.float32).copy()
-        for r in range(1, x.shape[0]):
-            acc = (acc + x[r]).astype(np.float32)
+        acc = x[:, 0].astype(np.float32).copy()
+        for r in range(1, x.shape[1]):
+            acc = (acc + x[:, r]).astype(np.float32)
         s = acc
     elif model in ("tw4", "tw8"):
         W = 4 if model == "tw4" else 8
@@ -98,18 +97,24 @@ def _mean_tile(x: np.ndarray, n_valid: int, dt: str, model: str) -> np.ndarray:
         for w in range(W):
             pair = []
             for l in range(2):
-                acc = x[2 * w + l].copy()
-                for rep in range(1, x.shape[0] // step):
-                    acc = round_to(acc + x[rep * step + 2 * w + l], dt)
+                acc = x[:, 2 * w + l].copy()
+                for rep in range(1, x.shape[1] // step):
+                    acc = round_to(acc + x[:, rep * step + 2 * w + l], dt)
                 pair.append(acc)
             parts.append(round_to(pair[0] + pair[1], dt))
-        while len(parts) > 1:
-            parts = [round_to(parts[i] + parts[i + 1], dt) for i in range(0, len(parts), 2)]
+        # warp partials are combined with xor shuffles of decreasing distance (W/2, ..., 1)
+        n = W // 2
+        while n >= 1:
+            parts = [round_to(parts[w] + parts[w ^ n], dt) for w in range(W)]
+            n //= 2
         s = parts[0]
     else:
         raise ValueError(model)
-    n = np.float32(n_valid)
-    return round_to(s.astype(np.float32) / n, dt)
+    nv = n_valid.astype(np.float32).reshape((-1,) + (1,) * (s.ndim - 1))
+    with np.errstate(invalid="ignore", divide="ignore"):
+        out = round_to(s.astype(np.float32) / nv, dt)
+    out[n_valid <= 0] = 0.0
+    return out
 
 
 def block_mean(k: np.ndarray, cu_seqlens, dt: str, model: str, block: int = 128):
@@ -118,34 +123,48 @@ def block_mean(k: np.ndarray, cu_seqlens, dt: str, model: str, block: int = 128)
     T, HK, D = k.shape
     mk = np.zeros((ntiles, HK, D), np.float32)
     for (start, L, nb, base) in layout:
-        for kb in range(nb):
-            r0 = kb * block
-            n_valid = min(block, L - r0)
-            tile = np.zeros((block, HK, D), np.float32)
-            tile[:n_valid] = k[start + r0:start + r0 + n_valid]
-            for h in range(HK):
-                mk[base + kb, h] = _mean_tile(tile[:, h, :], n_valid, dt, model)
+        if nb == 0:
+            continue
+        tiles = np.zeros((nb * block, HK, D), np.float32)
+        tiles[:L] = k[start:start + L]
+        tiles = tiles.reshape(nb, block, HK, D)
+        n_valid = np.minimum(block, L - np.arange(nb) * block)
+        mk[base:base + nb] = _mean_tiles(tiles, n_valid, dt, model)
     return mk
 
 
 # ------------------------------------------------------------------- block scores
-def block_scores_row(qblk: np.ndarray, mk_h: np.ndarray, qb: int, c: np.float32, all_tiles: bool):
-    """(m, p) for one query block against pooled keys kb = 0..qb -- native:129-188.
+def block_scores_head(qh: np.ndarray, mk_h: np.ndarray, nb: int, c: np.float32, qbs=None):
+    """(m, p) for the query blocks of one head -- native:129-188.
 
-    qblk: (128, D) zero padded; mk_h: (>=qb+1, D).  Row r is causal for kb iff
-    qb*128 + r >= kb*128 + 127 (native:157), so the diagonal block sees only row 127.
+    qh: (nb*128, D) zero padded queries of the head; mk_h: (nb, D).  Returns m, p of shape
+    (nb, nb) with m = -inf, p = 0 for kb > qb.  Row r of block qb is causal for kb iff
+    qb*128 + r >= kb*128 + 127 (native:157): the diagonal block sees only row 127, and
+    zero-padded rows past the end of the sequence count (their score is 0).
     """
-    nk = qb + 1
-    s = (qblk.astype(np.float64) @ mk_h[:nk].astype(np.float64).T).astype(np.float32)  # (128, nk)
-    s = (s * c).astype(np.float32)
-    m = s.max(axis=0)
-    m[qb] = s[127, qb]
-    d = (s - m[None, :]).astype(np.float32)
-    with np.errstate(over="ignore"):
-        e = np.exp2(d).astype(np.float32)
-    p = e[:, :qb].sum(axis=0, dtype=np.float32) if qb > 0 else np.zeros(0, np.float32)
-    p = np.concatenate([p, np.ones(1, np.float32)])
-    return m.astype(np.float32), p.astype(np.float32)
+    B = 128
+    m = np.full((nb, nb), -np.inf, np.float32)
+    p = np.zeros((nb, nb), np.float32)
+    qbs = list(range(nb) if qbs is None else qbs)
+    for c0 in range(0, len(qbs), 32):
+        blk = np.array(qbs[c0:c0 + 32])
+        rows = (blk[:, None] * B + np.arange(B)[None, :]).reshape(-1)
+        hi = int(blk.max()) + 1
+        s = (qh[rows].astype(np.float64) @ mk_h[:hi].astype(np.float64).T).astype(np.float32)
+        s = (s * c).astype(np.float32).reshape(len(blk), B, hi)
+        kb = np.arange(hi)
+        causal = kb[None, :] < blk[:, None]               # off-diagonal: every row counts
+        mm = s.max(axis=1)                                 # (nblk, hi)
+        diag_val = s[np.arange(len(blk)), B - 1, blk]      # row 127 of the diagonal block
+        mm = np.where(causal, mm, -np.inf).astype(np.float32)
+        mm[np.arange(len(blk)), blk] = diag_val
+        with np.errstate(over="ignore", invalid="ignore"):
+            e = np.exp2((s - mm[:, None, :]).astype(np.float32)).astype(np.float32)
+        pp = np.where(causal, e.sum(axis=1, dtype=np.float32), 0.0).astype(np.float32)
+        pp[np.arange(len(blk)), blk] = 1.0
+        m[blk, :hi] = mm
+        p[blk, :hi] = pp
+    return m, p
 
 
 # ------------------------------------------------------------------- selection
@@ -204,12 +223,17 @@ def search(q: np.ndarray, k: np.ndarray, cu_seqlens, hq: int, hk: int, *, dt: st
         qpad = np.zeros((nb * block, hq, D), np.float32)
         qpad[:L] = q[start:start + L]
         for h in range(hq):
-            mk_h = mk[base:base + nb, h // G]
-            for qb in range(nb):
-                if rows is not None and (si, h, qb) not in rows:
+            qbs = None
+            if rows is not None:
+                qbs = [qb for qb in range(nb) if (si, h, qb) in rows]
+                if not qbs:
                     continue
-                m, p = block_scores_row(qpad[qb * block:(qb + 1) * block, h], mk_h, qb, c, True)
-                s_, sc, t = select_row(m, p, qb, nb, alpha, sink, window, last_n, dense, min_budget)
+            if nb == 0:
+                continue
+            m, p = block_scores_head(qpad[:, h], mk[base:base + nb, h // G], nb, c, qbs)
+            for qb in (range(nb) if qbs is None else qbs):
+                s_, sc, t = select_row(m[qb, :qb + 1], p[qb, :qb + 1], qb, nb, alpha, sink, window, last_n,
+                                       dense, min_budget)
                 sel[h, qb] = s_
                 score[h, qb] = sc
                 thr[h, qb] = t
