@@ -1,0 +1,420 @@
+"""Benchmark of the sparse-prefill operator on B200 (one attention layer per step).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload l128k|cfg1|cfg2|cfg3]
+                    [--impl ours|reference]
+
+Default workload: the 128K-token Llama-3-8B-shaped layer the headline metric is quoted on
+(S=131072, 32 query / 8 KV heads, head_dim 128, bf16, alpha 0.18, sink 2, window 4,
+last_n 2).  Under torchrun (N>1) each rank owns a contiguous group of KV heads (and their
+query heads) of the SAME layer -- heads shard with no cross-GPU dependency -- so total work
+is fixed and the reported ms/layer is the max over ranks ("scaling": "strong").
+
+Timed region (``value``): K steps of the operator on inputs already in HBM (1.6 GB at
+128K, larger than the 126 MB L2, so no extra flush), CUDA events on the launching stream,
+barrier + synchronize on both sides, max over ranks.  ``e2e``: the same step through the
+public API ``flash_prefill`` with the inputs copied from pinned host memory and the output
+copied back inside the timed region.  ``roofline``: the attention kernel (dominant) against
+the measured dense bf16 peak; ``roofline_search``: the search stage against measured HBM
+bandwidth.  ``cpu_baseline``: the CPU restatement (oracle) on a bounded sample of the same
+layer, extrapolated to the whole layer.
+
+``--impl reference``: the reference implementation has no CPU path of its own (its Triton
+kernels only run on CPU through the interpreter, and its sources are not shipped to the
+GPU host), so this arm times the CPU restatement of the reference algorithm (``oracle/``)
+with every host thread on a bounded sample of the same layer, extrapolated to ms/layer.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "sparse-prefill attn ms/layer @128K on 1/8 B200; TC util; mask exactness"
+UNIT = "ms/layer"
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained"), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.25)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        finally:
+            try:
+                os.unlink(self.path)
+            except OSError:
+                pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [v for v in (num(r[1]) for r in rows) if v is not None]
+        mx = [v for v in (num(r[2]) for r in rows) if v is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        load = [s for s in sm if mx and s > 0.5 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------- workloads
+def workload(name):
+    from flashprefill_b200.synthetic import workloads
+    return workloads()[name]
+
+
+def device_inputs(w, hk0, hk1, device, seed):
+    """Inputs of KV heads [hk0, hk1) (and their query heads), generated on the device with
+    the recipe of flashprefill_b200.synthetic (same distribution, device RNG)."""
+    import torch
+    G = w.hq // w.hk
+    nh_q, nh_k = (hk1 - hk0) * G, hk1 - hk0
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    T = sum(w.seqlens)
+    D = w.d
+    q = torch.randn(T, nh_q, D, device=device, generator=g)
+    k = torch.randn(T, nh_k, D, device=device, generator=g)
+    v = torch.randn(T, nh_k, D, device=device, generator=g)
+    gc = torch.Generator(device=device)
+    gc.manual_seed(w.config_index * 1000 + 17)  # offset vector shared by every head and rank
+    off = 2.0 * torch.randn(D, device=device, generator=gc)
+    inv = 1.0 / (w.rope_base ** (torch.arange(0, D, 2, device=device, dtype=torch.float64) / D))
+    a = 0
+    for L in w.seqlens:
+        b = a + L
+        pos = torch.arange(L, device=device, dtype=torch.float64)
+        f = torch.outer(pos, inv)
+        emb = torch.cat([f, f], -1)
+        cos, sin = emb.cos().float()[:, None, :], emb.sin().float()[:, None, :]
+        for t in (q, k):
+            x = t[a:b] + off
+            x1, x2 = x[..., : D // 2], x[..., D // 2:]
+            t[a:b] = x * cos + torch.cat([-x2, x1], -1) * sin
+        k[a:a + 4] *= 8.0
+        nh = int(round(w.heavy_frac * L))
+        if nh:
+            idx = torch.randperm(L, device=device, generator=g)[:nh] + a
+            k[idx] *= 4.0
+        a = b
+    return q.to(w.dtype), k.to(w.dtype), v.to(w.dtype)
+
+
+def algorithmic(w, hq, hk, E):
+    """Algorithmic bytes of the search and FLOPs of search / attention for hq/hk local heads."""
+    T = sum(w.seqlens)
+    D = w.d
+    nbs = [math.ceil(L / 128) for L in w.seqlens]
+    search_bytes = 2 * (T * hq * D + T * hk * D) + 4 * E + 4 * hq * sum(nbs)
+    attn_flops = E * 4 * 128 * 128 * D
+    search_flops = hq * sum(nb * (nb + 1) // 2 for nb in nbs) * 2 * 128 * D
+    return search_bytes, attn_flops, search_flops
+
+
+# --------------------------------------------------------------------------- CPU arm
+def cpu_sample(w, seconds_budget=20.0):
+    """Time the CPU restatement on a bounded sample of the layer and extrapolate.
+
+    Sample: KV head 0 with its query heads of the longest sequence; pooled keys for the
+    whole sequence; search on random query blocks of head 0; attention on the selected
+    block pairs of those rows.  Search time scales with the number of (head, query block)
+    rows of the layer, attention time with the executed block pairs (estimated from the
+    sampled rows' density).  Returns (ms_per_layer, info)."""
+    import numpy as np
+    import torch
+
+    from flashprefill_b200.synthetic import make_sequence
+    from oracle import restate
+
+    L = max(w.seqlens)
+    G = w.hq // w.hk
+    q, k, v = make_sequence(L, G, 1, w.d, w.rope_base, w.heavy_frac, w.seed(0), torch.bfloat16)
+    f = lambda t: t.float().numpy()
+    qn, kn, vn = f(q), f(k), f(v)
+    nb = math.ceil(L / 128)
+    cu = np.array([0, L])
+    t0 = time.perf_counter()
+    mk = restate.block_mean(kn, cu, "bf16", "tw4")
+    t_mean = time.perf_counter() - t0
+    c = restate.scale_log2(w.d)
+    qpad = np.zeros((nb * 128, G, w.d), np.float32)
+    qpad[:L] = qn
+    order = np.random.default_rng(0).permutation(nb)
+    done, t_search, sel_rows = 0, 0.0, {}
+    while done < nb and t_search < seconds_budget * 0.5:
+        chunk = sorted(order[done:done + 16].tolist())
+        t1 = time.perf_counter()
+        m, p = restate.block_scores_head(qpad[:, 0], mk[:, 0], nb, c, chunk)
+        for qb in chunk:
+            s_, _, _ = restate.select_row(m[qb, :qb + 1], p[qb, :qb + 1], qb, nb, w.alpha, 2, 4, 2, True)
+            sel_rows[qb] = s_
+        t_search += time.perf_counter() - t1
+        done += len(chunk)
+    sel = np.zeros((1, nb, nb), bool)
+    for qb, s_ in sel_rows.items():
+        sel[0, qb] = s_
+    pairs, t_attn = 0, 0.0
+    for qb in sorted(sel_rows):
+        if t_attn > seconds_budget * 0.5:
+            break
+        t1 = time.perf_counter()
+        restate.sparse_attention(qn[:, :1], kn, vn, cu, [sel], 1, 1, rows={(0, 0, qb)})
+        t_attn += time.perf_counter() - t1
+        pairs += int(sel[0, qb].sum())
+    dens = sum(int(s.sum()) for s in sel_rows.values()) / max(1, done)
+    total_rows = w.hq * sum(math.ceil(x / 128) for x in w.seqlens)
+    E_est = dens * total_rows
+    ms = 1e3 * (t_mean * w.hk * (sum(w.seqlens) / L) + t_search / done * total_rows
+                + (t_attn / max(1, pairs)) * E_est)
+    info = {"sample": f"KV head 0 + its {G} query heads of one {L}-token sequence: pooled keys of all {nb} "
+                      f"blocks, search on {done} random query blocks of one head, attention on {pairs} block "
+                      f"pairs; extrapolated to {total_rows} (head, block) rows and E~{int(E_est)} pairs",
+            "cores": os.cpu_count()}
+    return ms, info
+
+
+# --------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="l128k")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    a = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    w = workload(a.workload)
+
+    if a.impl == "reference":
+        if rank != 0:
+            return
+        ms, info = cpu_sample(w, seconds_budget=max(10.0, 60.0 / max(1, a.steps)))
+        line = {"metric": METRIC, "value": round(ms, 3), "unit": UNIT, "n_gpus": a.gpus, "steps": 1,
+                "warmup": 0, "ms_per_step": round(ms, 3), "higher_is_better": False, "scaling": "strong",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded generator, BASELINE recipe)",
+                "impl": "reference",
+                "config": {"workload": w.name, "seq_len": sum(w.seqlens), "q_heads": w.hq, "kv_heads": w.hk,
+                           "head_dim": w.d, "alpha": w.alpha, "l2": "inputs larger than L2"},
+                "cpu_baseline": {"value": round(ms, 3), "unit": UNIT, "cores": info["cores"], "kind": "port",
+                                 "sample": info["sample"]},
+                "e2e": {"value": round(ms, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                "note": "the reference has no CPU path of its own; this is the CPU restatement of its algorithm"}
+        print(json.dumps(line))
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import flashprefill_b200 as fp
+    from flashprefill_b200 import _ops
+
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"))
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    if w.hk % world:
+        raise SystemExit(f"{w.hk} KV heads do not split over {world} ranks")
+    per = w.hk // world
+    hk0, hk1 = rank * per, (rank + 1) * per
+    G = w.hq // w.hk
+    hq_l, hk_l = per * G, per
+
+    q, k, v = device_inputs(w, hk0, hk1, dev, seed=w.config_index * 1000 + 1 + hk0)
+    T = q.shape[0]
+    cu = torch.tensor([0] + torch.tensor(w.seqlens).cumsum(0).tolist(), dtype=torch.int32, device=dev)
+    maxlen = max(w.seqlens)
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream(dev)
+    if w.varlen:
+        L = _ops.varlen_layout(len(w.seqlens), T, maxlen, hq_l, hk_l)
+    else:
+        L = _ops.dense_layout(1, T, hq_l, hk_l)
+    ws = torch.empty(L["total"], dtype=torch.uint8, device=dev)
+
+    def step(mid_event=None):
+        if w.varlen:
+            fp.search_varlen(q, k, cu, maxlen, w.alpha, 128, 2, 4, 2, workspace=ws)
+        else:
+            fp.search_dense(q[None], k[None], 128, 2, 4, w.alpha, 2, 0, workspace=ws)
+        if mid_event is not None:
+            mid_event.record(stream)
+        if w.varlen:
+            _ops.attention_varlen(q, k, v, out, cu, maxlen, ws)
+        else:
+            _ops.attention_dense(q[None], k[None], v[None], out[None], ws)
+
+    for _ in range(max(3, a.warmup)):
+        step()
+    torch.cuda.synchronize()
+    fp.check_device_error(ws)
+    cnt = ws[L["cnt"]:L["cnt"] + 4 * hq_l * L["tiles"]].view(torch.int32)
+    E_local = int(cnt.sum().item())
+
+    # ---- timed region (device-resident inputs)
+    evs = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(a.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t_wall = time.perf_counter()
+        for e0, e1, e2 in evs:
+            e0.record(stream)
+            step(e1)
+            e2.record(stream)
+        torch.cuda.synchronize()
+        t_wall = time.perf_counter() - t_wall
+    if world > 1:
+        dist.barrier()
+    clocks = clk.summary()
+    t_search = sum(e0.elapsed_time(e1) for e0, e1, e2 in evs) / a.steps
+    t_attn = sum(e1.elapsed_time(e2) for e0, e1, e2 in evs) / a.steps
+    t_step = sum(e0.elapsed_time(e2) for e0, e1, e2 in evs) / a.steps
+    stats = torch.tensor([t_step, t_search, t_attn, E_local], dtype=torch.float64, device=dev)
+    mx, tot = stats.clone(), stats.clone()
+    if world > 1:
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+    ms = float(mx[0])
+    E_total = int(tot[3])
+
+    # ---- end-to-end through the public API with host buffers
+    e2e = None
+    if not a.no_e2e:
+        hq_, hk_, hv_ = q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()
+        hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        dq, dk, dv, dout = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(out)
+
+        def e2e_step():
+            dq.copy_(hq_, non_blocking=True)
+            dk.copy_(hk_, non_blocking=True)
+            dv.copy_(hv_, non_blocking=True)
+            if w.varlen:
+                fp.flash_prefill_varlen_func(dq, dk, dv, dout, cu, maxlen, w.alpha, 128, 2, 4, 2)
+            else:
+                fp.flash_prefill(dq[None], dk[None], dv[None], dout[None], 128, 2, 4, w.alpha, 2, 0)
+            hout.copy_(dout, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        n_e2e = max(2, min(a.steps, 5))
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        s1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = torch.tensor([s0.elapsed_time(s1) / n_e2e], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(float(e2e_ms), 3), "unit": UNIT,
+               "h2d_bytes_per_step": int((q.numel() + k.numel() + v.numel()) * q.element_size() * world),
+               "d2h_bytes_per_step": int(out.numel() * out.element_size() * world), "steps": n_e2e}
+
+    # ---- CPU baseline (rank 0, N=1 only)
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu:
+        cms, info = cpu_sample(w, seconds_budget=20.0)
+        cpu = {"value": round(cms, 3), "unit": UNIT, "cores": info["cores"], "kind": "port", "sample": info["sample"]}
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    hbm, tflops, _, peak_kind = load_peaks()
+    sb, af, sf = algorithmic(w, hq_l, hk_l, E_local)
+    t_a, t_s = float(mx[2]), float(mx[1])
+    ach = af / (t_a * 1e-3) / 1e12
+    roof = {"bound": "tensor", "achieved": round(ach, 2), "peak": tflops, "unit": "TFLOP/s",
+            "frac": round(ach / tflops, 4), "traffic": None, "kernel": "sparse_attn_kernel", "ms": round(t_a, 4),
+            "algorithmic": f"E*4*128*128*128 FLOP, E={E_local} executed block pairs on this rank",
+            "peak_kind": f"{peak_kind} burst bf16 (of measured)" if peak_kind == "measured" else "fallback"}
+    sach = sb / (t_s * 1e-3) / 1e9
+    roof_s = {"bound": "hbm", "achieved": round(sach, 1), "peak": hbm, "unit": "GB/s", "frac": round(sach / hbm, 4),
+              "ms": round(t_s, 4), "mma_tflops": round(sf / (t_s * 1e-3) / 1e12, 1),
+              "kernels": "block_mean_kernel + block_search_kernel",
+              "algorithmic": "2*(S*Hq*D + S*Hk*D) + 4*E + 4*Hq*NB bytes", "peak_kind": f"{peak_kind} HBM copy"}
+    nbs = [math.ceil(L_ / 128) for L_ in w.seqlens]
+    P_pairs = w.hq * sum(nb * (nb + 1) // 2 for nb in nbs)
+    line = {"metric": METRIC, "value": round(ms, 4), "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": max(3, a.warmup), "ms_per_step": round(ms, 4), "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (BASELINE generator recipe, device RNG)",
+            "config": {"workload": w.name, "seq_len": sum(w.seqlens), "seqlens": w.seqlens, "q_heads": w.hq,
+                       "kv_heads": w.hk, "head_dim": w.d, "alpha": w.alpha, "sink": 2, "window": 4, "last_n": 2,
+                       "parallelism": f"kv-head groups x{world}", "l2": "inputs larger than L2 (no flush)"},
+            "search_ms": round(t_s, 4), "attention_ms": round(t_a, 4),
+            "executed_pairs": E_total, "density": round(E_total / P_pairs, 5),
+            "roofline": roof, "roofline_search": roof_s, "e2e": e2e, "cpu_baseline": cpu,
+            "gpu_launches": a.steps * (3 + (1 if w.varlen else 0)),
+            "clocks": clocks, "wall_s_timed": round(t_wall, 3)}
+    print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
