@@ -479,3 +479,5 @@ int fpb_read_device_error(const void* workspace, uint32_t* flags, void* stream) 
 }
 
 }  // extern "C"
+
+#include "fp_noalloc.cu"

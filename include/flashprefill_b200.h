@@ -132,6 +132,22 @@ FPB_API int fpb_attention_varlen(const void* q, const void* k, const void* v, vo
                                  const int64_t* v_strides, const int64_t* o_strides, int block_size,
                                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* Dense prefill that allocates nothing, for callers that cannot call cudaMalloc or pass
+ * a workspace (runtimes that forbid allocation on their hot path, hosts without a device
+ * allocator).  No counterpart in the reference.  Same arguments and results as
+ * fpb_prefill_dense without the workspace: it uses a 32 MiB device array inside the
+ * library, held by every GPU that loads the library until exit.  Problems whose
+ * workspace (fpb_dense_workspace_bytes) exceeds 32 MiB are rejected with FPB_EINVAL
+ * (e.g. 32K tokens with 32/8 heads fit; 128K do not).  The first call on a device looks
+ * up the array's address on that device and should come before any stream capture.
+ * Calls share the array: calls that overlap on the GPU race. */
+FPB_API int fpb_prefill_dense_noalloc(const void* q, const void* k, const void* v, void* out, int dtype, int batch,
+                                      int seqlen, int hq, int hk, int head_dim, const int64_t* q_strides,
+                                      const int64_t* k_strides, const int64_t* v_strides,
+                                      const int64_t* o_strides, int block_size, int attention_sink,
+                                      int window_size, float alpha, int last_n_block_full, int min_budget,
+                                      int mean_model, void* stream);
+
 /* Synchronises `stream`, copies the device error word of `workspace` to *flags and
  * returns FPB_EDEVICE if any bit is set.  No counterpart in the reference, which has no
  * device-side error reporting. */
