@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -144,6 +145,24 @@ int check_common(int dtype, int hq, int hk, int head_dim, int block_size) {
   return FPB_OK;
 }
 
+// Work-item counter of the persistent attention kernel (inside the 256-byte error block).
+constexpr int64_t kCounterOffset = 64;
+
+int sm_count(int* out) {
+  int dev = 0;
+  FPB_CUDA(cudaGetDevice(&dev));
+  static int cache[64] = {};
+  if (dev >= 0 && dev < 64 && cache[dev] > 0) {
+    *out = cache[dev];
+    return FPB_OK;
+  }
+  int n = 0;
+  FPB_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+  if (dev >= 0 && dev < 64) cache[dev] = n;
+  *out = n;
+  return FPB_OK;
+}
+
 template <typename KernelT>
 int set_smem(KernelT kernel, size_t bytes) {
   FPB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
@@ -248,16 +267,34 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
   AttnArgs A{};
   A.P = P;
   A.c = score_scale();
-  A.rescale_thr = kRescaleThreshold;
-  if (const char* e = std::getenv("FLASHPREFILL_B200_RESCALE_THRESHOLD")) A.rescale_thr = (float)std::atof(e);
+  A.pairs = (g.hq + 1) / 2;
+  if (std::getenv("FLASHPREFILL_B200_SINGLE_TILE")) A.pairs = -g.hq;  // debug: one head per item
+  A.total_items = L.tiles * (A.pairs < 0 ? -A.pairs : A.pairs);
+  A.counter = reinterpret_cast<int*>(ws + L.err + kCounterOffset);
+  FPB_CUDA(cudaMemsetAsync(A.counter, 0, sizeof(int), stream));
   A.idx = reinterpret_cast<const int32_t*>(ws + L.idx);
   A.cnt = reinterpret_cast<const int32_t*>(ws + L.cnt);
   A.out = o;
   A.o_sb = os[0];
   A.o_ss = os[1];
   A.o_sh = os[2];
+  A.profile = std::getenv("FLASHPREFILL_B200_PROFILE") != nullptr;
+  if (A.profile) {
+    static const unsigned long long zeros[kProfSlots] = {};
+    FPB_CUDA(cudaMemcpyToSymbolAsync(g_attn_prof, zeros, sizeof(zeros), 0, cudaMemcpyHostToDevice, stream));
+  }
+  {
+    cudaFuncAttributes fa{};
+    FPB_CUDA(cudaFuncGetAttributes(&fa, g.dtype == FPB_BF16 ? (const void*)sparse_attn_kernel<__nv_bfloat16>
+                                                             : (const void*)sparse_attn_kernel<__half>));
+    if (fa.numRegs != kAttnLaunchRegs)
+      return fail(FPB_ECUDA, "attention kernel compiled with %d registers/thread, %d expected by its register split",
+                  fa.numRegs, kAttnLaunchRegs);
+  }
   const size_t smem = attn_smem_bytes();
-  const unsigned grid = (unsigned)L.tiles * (unsigned)g.hq;
+  int sms = 0;
+  FPB_TRY(sm_count(&sms));
+  const unsigned grid = (unsigned)std::min(sms, A.total_items);
   if (g.dtype == FPB_BF16) {
     FPB_TRY(set_smem(sparse_attn_kernel<__nv_bfloat16>, smem));
     sparse_attn_kernel<__nv_bfloat16><<<grid, kAttnThreads, smem, stream>>>(tm_q, tm_k, tm_v, tm_o, A);
@@ -266,6 +303,18 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
     sparse_attn_kernel<__half><<<grid, kAttnThreads, smem, stream>>>(tm_q, tm_k, tm_v, tm_o, A);
   }
   FPB_CUDA(cudaGetLastError());
+  if (A.profile) {  // debug instrumentation: synchronises and prints per-phase cycle sums
+    unsigned long long h[kProfSlots];
+    FPB_CUDA(cudaMemcpyFromSymbolAsync(h, g_attn_prof, sizeof(h), 0, cudaMemcpyDeviceToHost, stream));
+    FPB_CUDA(cudaStreamSynchronize(stream));
+    static const char* names[kProfSlots] = {
+        "mma_wait_p_full", "mma_wait_k_full", "mma_wait_v_full", "mma_wait_q_full+o_empty", "mma_wait_item",
+        "sm_wait_s_full", "sm_wait_o_full", "sm_wait_item", "sm_pass1", "sm_rescale", "sm_pass2", "sm_epilogue",
+        "sm_epi_sync", "k_wait_k_empty", "k_wait_q_empty", "k_wait_item_empty", "v_wait_v_empty", "v_wait_item",
+        "cta_total_cycles", "items", "softmax_block_iters", "rescales", "sm_tmem_ld_S", "sm_tmem_st_P_wait"};
+    fprintf(stderr, "[fpb profile] grid=%u\n", grid);
+    for (int i = 0; i < kProfSlots; ++i) fprintf(stderr, "[fpb profile] %-26s %llu\n", names[i], h[i]);
+  }
   return FPB_OK;
 }
 

@@ -60,6 +60,17 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe (never suspends the thread).
+__device__ __forceinline__ bool mbar_probe(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete.  Returns false on timeout or
 // when another thread of the CTA has raised *abort (the CTA is shutting down).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
@@ -77,10 +88,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 
 // Warp-uniform variant for warps whose lanes then execute warp-collective instructions
 // (tcgen05.ld/st, shuffles): every lane returns the same value.
+template <bool kProbe = false>
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort) {
   const uint64_t t0 = global_timer_ns();
   while (true) {
-    const bool done = mbar_test(bar, parity);
+    const bool done = kProbe ? mbar_probe(bar, parity) : mbar_test(bar, parity);
     if (__all_sync(0xffffffffu, done)) return true;
     const bool stop = (*abort != 0) || (global_timer_ns() - t0 > kWaitLimitNs);
     if (__any_sync(0xffffffffu, stop)) {
@@ -111,6 +123,11 @@ __device__ __forceinline__ void tma_load_4d_hint(void* dst, const CUtensorMap* m
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3) {
@@ -219,6 +236,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       FPB_W32(r)
       : "memory");
 }
+#define FPB_W16(a)                                                                                               \
+  "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]), "r"(a[6]), "r"(a[7]), "r"(a[8]), "r"(a[9]), \
+      "r"(a[10]), "r"(a[11]), "r"(a[12]), "r"(a[13]), "r"(a[14]), "r"(a[15])
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      FPB_W16(r)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -228,6 +255,54 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// ---- packed fp32 pairs (sm_100 f32x2 instructions) and 3-input max
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0, float c1) {
+  asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n mov.b64 rc, {%6, %7};\n"
+      " fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0, %1}, rd;\n}\n"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void add2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+      " add.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}\n"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair of x <= 0 on the FMA pipe (takes load off the 16/clk/SM MUFU unit).
+// Cody-Waite style split x = n + f with n = round(x) (adding 1.5*2^23 rounds to an integer)
+// and f in [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients were fitted here
+// for minimal relative error with the constant term fixed to 1 (so 2^0 = 1 exactly; max
+// relative error 1.0e-4, far below the 2^-9 of the bf16 P it feeds); 2^n is applied by
+// adding n to the exponent field.  x is clamped at -126 (the result there is < 2^-125).
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  constexpr float C1 = 0.6932829022407532f, C2 = 0.2422109693288803f, C3 = 0.05500892922282219f;
+  x0 = fmaxf(x0, -126.f);
+  x1 = fmaxf(x1, -126.f);
+  float j0, j1, t0, t1, f0, f1, p0, p1;
+  add2(j0, j1, x0, x1, kShift, kShift);
+  add2(t0, t1, j0, j1, -kShift, -kShift);
+  fma2(f0, f1, t0, t1, -1.f, -1.f, x0, x1);
+  fma2(p0, p1, C3, C3, f0, f1, C2, C2);
+  fma2(p0, p1, p0, p1, f0, f1, C1, C1);
+  fma2(p0, p1, p0, p1, f0, f1, 1.f, 1.f);
+  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(j0) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(j1) << 23));
+}
+
+// Register reallocation between warpgroups.  The sum over the CTA must not exceed the
+// registers the CTA was launched with (the host checks the kernel's register count).
+template <int N>
+__device__ __forceinline__ void regs_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
+template <int N>
+__device__ __forceinline__ void regs_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

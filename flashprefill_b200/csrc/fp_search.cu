@@ -49,7 +49,7 @@ constexpr uint32_t kHalfTile = kTileBytes / 2;
 
 __host__ __device__ constexpr size_t search_smem_bytes(int cap) {
   // Q + 2 pooled-key stages + m/p arrays + top-k marks + barriers/scalars + alignment slack
-  return 3 * (size_t)kTileBytes + 8 * (size_t)cap + (size_t)((cap + 31) / 32) * 4 + 256 + 1024;
+  return 3 * (size_t)kTileBytes + 8 * (size_t)cap + (size_t)((cap + 31) / 32) * 4 + 384 + 1024;
 }
 
 // Sum / max over the 128 epilogue threads (warps 2..5); uses named barrier 1.
@@ -114,6 +114,7 @@ __global__ void __launch_bounds__(kSearchThreads, 1)
   float* red = reinterpret_cast<float*>(tmem_slot + 4);   // 4 floats
   int* red_i = reinterpret_cast<int*>(tmem_slot + 8);     // 4 ints
   int* red_k = reinterpret_cast<int*>(tmem_slot + 12);    // 4 ints
+  int* failed_flag = reinterpret_cast<int*>(tmem_slot + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = qb / kBlock + 1;
@@ -129,6 +130,7 @@ __global__ void __launch_bounds__(kSearchThreads, 1)
     mbar_init(mma_done, 1);
     *abort = 0;
     *mrun = float_to_ordered(-INFINITY);
+    *failed_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -259,9 +261,12 @@ __global__ void __launch_bounds__(kSearchThreads, 1)
         p_arr[kb] = cand ? p : -1.f;
       }
     }
-    // ---- normalise, threshold, compact
+    // ---- normalise, threshold, compact (the failure decision is taken once for all 4 warps)
+    if (!ok) *failed_flag = 1;
     named_bar_sync(1, 128);
-    const bool failed = __any_sync(0xffffffffu, !ok || *abort);
+    if (et == 0 && *abort) *failed_flag = 1;
+    named_bar_sync(1, 128);
+    const bool failed = *(volatile int*)failed_flag != 0;
     if (failed) {
       if (et == 0) *out_cnt = 0;
     } else {
