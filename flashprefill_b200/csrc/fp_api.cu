@@ -267,9 +267,7 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
   AttnArgs A{};
   A.P = P;
   A.c = score_scale();
-  A.pairs = (g.hq + 1) / 2;
-  if (std::getenv("FLASHPREFILL_B200_SINGLE_TILE")) A.pairs = -g.hq;  // debug: one head per item
-  A.total_items = L.tiles * (A.pairs < 0 ? -A.pairs : A.pairs);
+  A.total_items = L.tiles * g.hq;
   A.counter = reinterpret_cast<int*>(ws + L.err + kCounterOffset);
   FPB_CUDA(cudaMemsetAsync(A.counter, 0, sizeof(int), stream));
   A.idx = reinterpret_cast<const int32_t*>(ws + L.idx);
@@ -308,9 +306,9 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
     FPB_CUDA(cudaMemcpyFromSymbolAsync(h, g_attn_prof, sizeof(h), 0, cudaMemcpyDeviceToHost, stream));
     FPB_CUDA(cudaStreamSynchronize(stream));
     static const char* names[kProfSlots] = {
-        "mma_wait_p_full", "mma_wait_k_full", "mma_wait_v_full", "mma_wait_q_full+o_empty", "mma_wait_item",
+        "mma_blk_p_full", "mma_blk_k_full", "mma_blk_v_full", "mma_blk_q_or_o", "mma_blk_item_or_issue",
         "sm_wait_s_full", "sm_wait_o_full", "sm_wait_item", "sm_pass1", "sm_rescale", "sm_pass2", "sm_epilogue",
-        "sm_epi_sync", "k_wait_k_empty", "k_wait_q_empty", "k_wait_item_empty", "v_wait_v_empty", "v_wait_item",
+        "sm_epi_sync", "prod_wait_k_empty", "prod_wait_q_empty", "prod_wait_item_empty", "prod_wait_v_empty", "mma_pipe_done",
         "cta_total_cycles", "items", "softmax_block_iters", "rescales", "sm_tmem_ld_S", "sm_tmem_st_P_wait"};
     fprintf(stderr, "[fpb profile] grid=%u\n", grid);
     for (int i = 0; i < kProfSlots; ++i) fprintf(stderr, "[fpb profile] %-26s %llu\n", names[i], h[i]);

@@ -7,18 +7,20 @@
 // dtype for the P V product, O = acc / l stored in the input dtype.  A row whose list is
 // empty outputs zeros (the reference starts l at 1.0 and acc at 0).
 //
-// Persistent kernel, one CTA per SM, 384 threads.  A work item is one query block of two
-// query heads ("tiles" a and b); items are handed out heavy-first by an atomic counter.
-//   warp 0      scheduler (fetches items into a 2-slot smem ring) + TMA producer of Q and K
-//   warp 1      TMEM owner + tcgen05.mma issuer
-//   warp 2      TMA producer of V
-//   warps 4-7   softmax / epilogue of tile a, warps 8-11 of tile b; one TMEM lane (= one
-//               query row) per thread
-// MMA issue order per item: S_a(0), S_b(0), then for each block j: PV_a(j), S_a(j+1),
-// PV_b(j), S_b(j+1).  The tensor core therefore works on one tile while the other tile's
-// softmax runs, and because PV_x(j) is issued before S_x(j+1), O_x is final whenever
-// S_x(j+1) completes: the exact running-max rescale of O (as in the reference) never waits.
-// TMEM columns: S_a [0,128), S_b [128,256), O_a [256,384), O_b [384,512).  P (16-bit
+// Persistent kernel, one CTA per SM, 384 threads, running two independent pipelines that
+// share the tensor core.  A work item is one (query block, query head); each pipeline
+// fetches its own items, heavy-first, from one atomic counter.
+//   warp 0 / warp 2   scheduler + TMA producer (Q, then K and V of each listed block)
+//                     of pipeline 0 / 1, with single-slot Q, K and V buffers
+//   warp 1            TMEM owner + tcgen05.mma issuer: a non-blocking state machine that
+//                     issues for whichever pipeline has its inputs ready (S_x(j) = Q K^T
+//                     when K_x(j) has landed; PV_x(j) when P_x(j) and V_x(j) are ready)
+//   warps 4-7 / 8-11  softmax / epilogue of pipeline 0 / 1; one TMEM lane (= one query
+//                     row) per thread
+// While one pipeline's softmax runs, the tensor core works for the other.  PV_x(j) is
+// issued before S_x(j+1), so O_x is final whenever S_x(j+1) completes: the exact
+// running-max rescale of O (as in the reference) never waits.
+// TMEM columns: S_0 [0,128), S_1 [128,256), O_0 [256,384), O_1 [384,512).  P (16-bit
 // pairs) is written over the first 64 columns of S and read by the TS-form MMA.
 // The largest P of a row is exactly 1.0, which keeps the bf16 rounding of P at the
 // reference's level (a lazy max that lets P grow above 1 adds up to one bf16 ulp of P).
@@ -33,8 +35,7 @@ struct AttnArgs {
   const int32_t* cnt;        // [hq][tiles_ub]
   int* counter;              // work-item counter, zero at launch
   int profile;               // accumulate g_attn_prof
-  int total_items;           // tiles_ub * pairs
-  int pairs;                 // ceil(hq / 2)
+  int total_items;           // tiles_ub * hq
   void* out;                 // output base (masked-store path)
   int64_t o_sb, o_ss, o_sh;  // output strides in elements
 };
@@ -74,13 +75,11 @@ constexpr uint32_t kAttnHalf = kAttnTile / 2;
 
 __host__ __device__ constexpr size_t attn_smem_bytes() { return (size_t)kAttnTile * 6 + 1024 + 1024; }
 
-// One work item as published by the scheduler in the smem ring.
+// One work item as published by a pipeline's scheduler in its smem ring.
 struct ItemInfo {
   int valid;  // 0: no more work, 1: item, 2: empty slot of the grid (skip)
-  int start, len, nb, tile_base, bcoord, qb;
-  int h[2];   // query heads of tiles a, b (-1: none)
-  int n[2];   // list lengths
-  int pad[3];
+  int start, len, tile_base, bcoord, qb, h, n, last_kb;
+  int pad[7];
 };
 
 template <typename T>
@@ -90,45 +89,45 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                        const AttnArgs A) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                   // [2] tiles
-  uint8_t* sK = smem + 2 * kAttnTile;   // [2] slots
-  uint8_t* sV = smem + 4 * kAttnTile;   // [2] slots
+  // pipeline x owns [x * 3 tiles): Q, K, V
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kAttnTile);
-  uint64_t* item_full = bars + 0;
-  uint64_t* item_empty = bars + 2;
-  uint64_t* q_full = bars + 4;
-  uint64_t* q_empty = bars + 6;
-  uint64_t* k_full = bars + 8;
-  uint64_t* k_empty = bars + 10;
-  uint64_t* v_full = bars + 12;
-  uint64_t* v_empty = bars + 14;
-  uint64_t* s_full = bars + 16;
-  uint64_t* p_full = bars + 18;
-  uint64_t* o_full = bars + 20;
-  uint64_t* o_empty = bars + 22;
-  uint64_t* mma_done = bars + 24;
-  uint64_t* epi = bars + 26;  // [2] bounded sync of a tile's 128 epilogue threads
-  ItemInfo* ring = reinterpret_cast<ItemInfo*>(bars + 28);  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring + 2);
+  uint64_t* item_full = bars + 0;    // [pipeline][slot]
+  uint64_t* item_empty = bars + 4;   // [pipeline][slot]
+  uint64_t* q_full = bars + 8;       // [pipeline]
+  uint64_t* q_empty = bars + 10;
+  uint64_t* k_full = bars + 12;
+  uint64_t* k_empty = bars + 14;
+  uint64_t* v_full = bars + 16;
+  uint64_t* v_empty = bars + 18;
+  uint64_t* s_full = bars + 20;
+  uint64_t* p_full = bars + 22;
+  uint64_t* o_full = bars + 24;
+  uint64_t* o_empty = bars + 26;
+  uint64_t* epi = bars + 28;         // bounded sync of a pipeline's 128 epilogue threads
+  uint64_t* mma_done = bars + 30;
+  ItemInfo* ring = reinterpret_cast<ItemInfo*>(bars + 32);  // [pipeline][slot]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring + 4);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   unsigned long long* prof_smem = reinterpret_cast<unsigned long long*>(tmem_slot + 4);  // [kProfSlots]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 4; ++i) {
       mbar_init(item_full + i, 1);
-      mbar_init(item_empty + i, 2 + 256);
-      mbar_init(q_full + i, 1);
-      mbar_init(q_empty + i, 1);
-      mbar_init(k_full + i, 1);
-      mbar_init(k_empty + i, 1);
-      mbar_init(v_full + i, 1);
-      mbar_init(v_empty + i, 1);
-      mbar_init(s_full + i, 1);
-      mbar_init(p_full + i, 128);
-      mbar_init(o_full + i, 1);
-      mbar_init(o_empty + i, 128);
-      mbar_init(epi + i, 128);
+      mbar_init(item_empty + i, 1 + 128);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(q_full + x, 1);
+      mbar_init(q_empty + x, 1);
+      mbar_init(k_full + x, 1);
+      mbar_init(k_empty + x, 1);
+      mbar_init(v_full + x, 1);
+      mbar_init(v_empty + x, 1);
+      mbar_init(s_full + x, 1);
+      mbar_init(p_full + x, 128);
+      mbar_init(o_full + x, 1);
+      mbar_init(o_empty + x, 128);
+      mbar_init(epi + x, 128);
     }
     mbar_init(mma_done, 1);
     *abort = 0;
@@ -147,244 +146,210 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   // one recording thread per role / per softmax warpgroup (threads 128 and 256)
   pa.sm = (A.profile && (threadIdx.x < 128 ? lane == 0 : (threadIdx.x & 127) == 0)) ? prof_smem : nullptr;
   const unsigned long long t_kernel0 = clk();
-
-  auto list_of = [&](const ItemInfo& f, int h) -> const int32_t* {
-    return A.idx + ((int64_t)h * A.P.tiles_ub + f.tile_base + f.qb) * A.P.cap;
-  };
+  const int group = A.P.hq / A.P.hk;
 
   if (warp < 4) {
   regs_dec<kAttnRoleRegs>();
-  if (warp == 0) {
-    // ------------------------------------------------------------ scheduler + Q/K producer
-    if (lane == 0) {
-      prefetch_tmap(&tm_q);
-      prefetch_tmap(&tm_k);
-      const uint64_t stream_once = l2_policy_evict_first();
-      uint32_t it = 0, kseq = 0, qld[2] = {0, 0};
-      while (true) {
-        const int slot = it & 1;
-        if (!FPB_TW(15, mbar_wait(item_empty + slot, ((it >> 1) & 1) ^ 1, abort))) break;
-        ItemInfo f{};
-        const int id = atomicAdd(A.counter, 1);
-        if (id >= A.total_items) {
-          f.valid = 0;
+  if ((warp == 0 || warp == 2) && lane == 0) {
+    // ------------------------------------------------------------ scheduler + producer of pipeline x
+    const int x = warp >> 1;
+    uint8_t* sQ = smem + x * 3 * kAttnTile;
+    uint8_t* sK = sQ + kAttnTile;
+    uint8_t* sV = sK + kAttnTile;
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+    const uint64_t stream_once = l2_policy_evict_first();
+    uint32_t it = 0, kseq = 0, vseq = 0, qld = 0;
+    bool ok = true;
+    while (ok) {
+      const int slot = it & 1;
+      if (!FPB_TW(15, mbar_wait(item_empty + 2 * x + slot, ((it >> 1) & 1) ^ 1, abort))) break;
+      ItemInfo f{};
+      const int id = atomicAdd(A.counter, 1);
+      const int32_t* lst = nullptr;
+      if (id >= A.total_items) {
+        f.valid = 0;
+      } else {
+        SeqInfo s;
+        int qb;
+        if (!decode_item(A.P, id / A.P.hq, s, qb)) {
+          f.valid = 2;
         } else {
-          SeqInfo s;
-          int qb;
-          const bool single = A.pairs < 0;
-          const int np = single ? -A.pairs : A.pairs;
-          const int pair = id % np;
-          if (!decode_item(A.P, id / np, s, qb)) {
-            f.valid = 2;
-          } else {
-            f.valid = 1;
-            f.start = s.start;
-            f.len = s.len;
-            f.nb = s.nb;
-            f.tile_base = s.tile_base;
-            f.bcoord = s.bcoord;
-            f.qb = qb;
-            for (int x = 0; x < 2; ++x) {
-              const int h = single ? (x == 0 ? pair : A.P.hq) : 2 * pair + x;
-              f.h[x] = h < A.P.hq ? h : -1;
-              int n = 0;
-              if (f.h[x] >= 0) n = __ldg(A.cnt + (int64_t)h * A.P.tiles_ub + s.tile_base + qb);
-              f.n[x] = max(0, min(n, qb + 1));
-            }
-          }
+          f.valid = 1;
+          f.start = s.start;
+          f.len = s.len;
+          f.tile_base = s.tile_base;
+          f.bcoord = s.bcoord;
+          f.qb = qb;
+          f.h = id % A.P.hq;
+          const int64_t row = (int64_t)f.h * A.P.tiles_ub + s.tile_base + qb;
+          f.n = max(0, min(__ldg(A.cnt + row), qb + 1));
+          lst = A.idx + row * A.P.cap;
+          f.last_kb = f.n > 0 ? __ldg(lst + f.n - 1) : -1;
         }
-        ring[slot] = f;
-        mbar_arrive(item_full + slot);
-        if (f.valid == 1) pa.add(19, 1);
-        ++it;
-        if (f.valid == 0) break;
-        if (f.valid == 2) continue;
-        const int qrow = f.start + f.qb * kBlock;
-        bool ok = true;
-        
-#pragma unroll
-        for (int x = 0; x < 2 && ok; ++x) {
-          if (f.h[x] < 0 || f.n[x] == 0) continue;
-          if (!FPB_TW(14, mbar_wait(q_empty + x, (qld[x] & 1) ^ 1, abort))) { ok = false; break; }
-          ++qld[x];
-          uint8_t* dst = sQ + x * kAttnTile;
-          mbar_arrive_expect_tx(q_full + x, kAttnTile);
-          tma_load_4d_hint(dst, &tm_q, q_full + x, 0, f.h[x], qrow, f.bcoord, stream_once);
-          tma_load_4d_hint(dst + kAttnHalf, &tm_q, q_full + x, 64, f.h[x], qrow, f.bcoord, stream_once);
-        }
-        const int hk[2] = {f.h[0] >= 0 ? f.h[0] / (A.P.hq / A.P.hk) : 0,
-                           f.h[1] >= 0 ? f.h[1] / (A.P.hq / A.P.hk) : 0};
-        const int32_t* lst[2] = {f.h[0] >= 0 ? list_of(f, f.h[0]) : nullptr, f.h[1] >= 0 ? list_of(f, f.h[1]) : nullptr};
-        const int nmax = max(f.n[0], f.n[1]);
-        for (int j = 0; j < nmax && ok; ++j) {
-#pragma unroll
-          for (int x = 0; x < 2; ++x) {
-            if (j >= f.n[x]) continue;
-            int kb = __ldg(lst[x] + j);
-            if (kb < 0 || kb > f.qb) {
-              raise_error(A.P.err, kErrIndexRange);
-              kb = f.qb;
-            }
-            const int sl = kseq & 1;
-            if (!FPB_TW(13, mbar_wait(k_empty + sl, ((kseq >> 1) & 1) ^ 1, abort))) { ok = false; break; }
-            ++kseq;
-            uint8_t* dst = sK + sl * kAttnTile;
-            const int krow = f.start + kb * kBlock;
-            mbar_arrive_expect_tx(k_full + sl, kAttnTile);
-            tma_load_4d(dst, &tm_k, k_full + sl, 0, hk[x], krow, f.bcoord);
-            tma_load_4d(dst + kAttnHalf, &tm_k, k_full + sl, 64, hk[x], krow, f.bcoord);
-          }
-        }
-        if (!ok) break;
       }
-      if (*abort) {  // let loads still in flight land before the CTA exits
-        volatile int no_abort = 0;
-        for (uint32_t s = (kseq > 2 ? kseq - 2 : 0); s < kseq; ++s) mbar_wait(k_full + (s & 1), (s >> 1) & 1, &no_abort);
-        for (int x = 0; x < 2; ++x)
-          if (qld[x]) mbar_wait(q_full + x, (qld[x] - 1) & 1, &no_abort);
+      ring[2 * x + slot] = f;
+      mbar_arrive(item_full + 2 * x + slot);
+      if (f.valid == 1) pa.add(19, 1);
+      ++it;
+      if (f.valid == 0) break;
+      if (f.valid == 2 || f.n == 0) continue;
+      const int hk = f.h / group;
+      if (!FPB_TW(14, mbar_wait(q_empty + x, (qld & 1) ^ 1, abort))) break;
+      ++qld;
+      const int qrow = f.start + f.qb * kBlock;
+      mbar_arrive_expect_tx(q_full + x, kAttnTile);
+      tma_load_4d_hint(sQ, &tm_q, q_full + x, 0, f.h, qrow, f.bcoord, stream_once);
+      tma_load_4d_hint(sQ + kAttnHalf, &tm_q, q_full + x, 64, f.h, qrow, f.bcoord, stream_once);
+      for (int j = 0; j < f.n; ++j) {
+        int kb = __ldg(lst + j);
+        if (kb < 0 || kb > f.qb) {
+          raise_error(A.P.err, kErrIndexRange);
+          kb = f.qb;
+        }
+        const int krow = f.start + kb * kBlock;
+        if (!FPB_TW(13, mbar_wait(k_empty + x, (kseq & 1) ^ 1, abort))) { ok = false; break; }
+        ++kseq;
+        mbar_arrive_expect_tx(k_full + x, kAttnTile);
+        tma_load_4d(sK, &tm_k, k_full + x, 0, hk, krow, f.bcoord);
+        tma_load_4d(sK + kAttnHalf, &tm_k, k_full + x, 64, hk, krow, f.bcoord);
+        if (!FPB_TW(16, mbar_wait(v_empty + x, (vseq & 1) ^ 1, abort))) { ok = false; break; }
+        ++vseq;
+        mbar_arrive_expect_tx(v_full + x, kAttnTile);
+        tma_load_4d(sV, &tm_v, v_full + x, 0, hk, krow, f.bcoord);
+        tma_load_4d(sV + kAttnHalf, &tm_v, v_full + x, 64, hk, krow, f.bcoord);
       }
     }
-  } else if (warp == 2) {
-    // ------------------------------------------------------------ V producer
-    if (lane == 0) {
-      prefetch_tmap(&tm_v);
-      uint32_t it = 0, vseq = 0;
-      while (true) {
-        const int slot = it & 1;
-        if (!FPB_TW(17, mbar_wait(item_full + slot, (it >> 1) & 1, abort))) break;
-        const ItemInfo f = ring[slot];
-        mbar_arrive(item_empty + slot);
-        ++it;
-        if (f.valid == 0) break;
-        if (f.valid == 2) continue;
-        bool ok = true;
-        const int nmax = max(f.n[0], f.n[1]);
-        for (int j = 0; j < nmax && ok; ++j) {
-#pragma unroll
-          for (int x = 0; x < 2; ++x) {
-            if (j >= f.n[x]) continue;
-            int kb = __ldg(list_of(f, f.h[x]) + j);
-            if (kb < 0 || kb > f.qb) kb = f.qb;
-            const int hk = f.h[x] / (A.P.hq / A.P.hk);
-            const int sl = vseq & 1;
-            if (!FPB_TW(16, mbar_wait(v_empty + sl, ((vseq >> 1) & 1) ^ 1, abort))) { ok = false; break; }
-            ++vseq;
-            uint8_t* dst = sV + sl * kAttnTile;
-            const int krow = f.start + kb * kBlock;
-            mbar_arrive_expect_tx(v_full + sl, kAttnTile);
-            tma_load_4d(dst, &tm_v, v_full + sl, 0, hk, krow, f.bcoord);
-            tma_load_4d(dst + kAttnHalf, &tm_v, v_full + sl, 64, hk, krow, f.bcoord);
-          }
-        }
-        if (!ok) break;
-      }
-      if (*abort) {
-        volatile int no_abort = 0;
-        for (uint32_t s = (vseq > 2 ? vseq - 2 : 0); s < vseq; ++s) mbar_wait(v_full + (s & 1), (s >> 1) & 1, &no_abort);
-      }
+    if (*abort) {  // let loads still in flight land before the CTA exits
+      volatile int no_abort = 0;
+      if (kseq) mbar_wait(k_full + x, (kseq - 1) & 1, &no_abort);
+      if (vseq) mbar_wait(v_full + x, (vseq - 1) & 1, &no_abort);
+      if (qld) mbar_wait(q_full + x, (qld - 1) & 1, &no_abort);
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t id_s = idesc_f16(128, 128, DT<T>::is_bf16, false);
-      constexpr uint32_t id_o = idesc_f16(128, 128, DT<T>::is_bf16, true);
-      uint32_t it = 0, kc = 0, vc = 0, qc[2] = {0, 0}, pc[2] = {0, 0}, oc[2] = {0, 0};
-      bool ok = true;
-      auto issue_s = [&](int x) -> bool {
-        const int sl = kc & 1;
-        if (!FPB_TW(1, mbar_wait(k_full + sl, (kc >> 1) & 1, abort))) return false;
-        ++kc;
-        tc_fence_after();
-        const uint32_t q_base = smem_u32(sQ + x * kAttnTile);
-        const uint32_t k_base = smem_u32(sK + sl * kAttnTile);
+    constexpr uint32_t id_s = idesc_f16(128, 128, DT<T>::is_bf16, false);
+    constexpr uint32_t id_o = idesc_f16(128, 128, DT<T>::is_bf16, true);
+    enum { kNeedItem = 0, kNeedS = 1, kNeedPV = 2, kDone = 3 };
+    int st[2] = {kNeedItem, kNeedItem}, jj[2] = {0, 0}, nn[2] = {0, 0};
+    uint32_t it[2] = {0, 0}, qc[2] = {0, 0}, kc[2] = {0, 0}, vc[2] = {0, 0}, pc[2] = {0, 0}, oc[2] = {0, 0};
+    uint64_t last_progress = global_timer_ns();
+    int why[2] = {4, 4};  // profile: reason each pipeline was blocked in the previous sweep
+    unsigned long long t_prev = clk();
+    while (st[0] != kDone || st[1] != kDone) {
+      bool progress = false;
+      if (pa.sm) {
+        const unsigned long long now = clk();
+        pa.add(why[0], now - t_prev);
+        pa.add(why[1], now - t_prev);
+        t_prev = now;
+      }
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t off = (ks >> 2) * kAttnHalf + (ks & 3) * 32;
-          umma_ss(tmem + x * 128, sdesc_sw128(q_base + off, 16, 1024), sdesc_sw128(k_base + off, 16, 1024), id_s,
-                  ks > 0);
+      for (int x = 0; x < 2; ++x) {
+        why[x] = st[x] == kDone ? 17 : 4;
+        if (st[x] == kNeedItem) {
+          const int slot = it[x] & 1;
+          if (mbar_probe(item_full + 2 * x + slot, (it[x] >> 1) & 1)) {
+            const ItemInfo f = ring[2 * x + slot];
+            mbar_arrive(item_empty + 2 * x + slot);
+            ++it[x];
+            progress = true;
+            if (f.valid == 0) st[x] = kDone;
+            else if (f.valid == 1 && f.n > 0) {
+              st[x] = kNeedS;
+              jj[x] = 0;
+              nn[x] = f.n;
+            }
+          }
         }
-        umma_commit(k_empty + sl);
-        umma_commit(s_full + x);
-        return true;
-      };
-      while (ok) {
-        const int slot = it & 1;
-        if (!FPB_TW(4, mbar_wait(item_full + slot, (it >> 1) & 1, abort))) break;
-        const ItemInfo f = ring[slot];
-        mbar_arrive(item_empty + slot);
-        ++it;
-        if (f.valid == 0) break;
-        if (f.valid == 2) continue;
-        bool act[2];
-        for (int x = 0; x < 2; ++x) act[x] = f.h[x] >= 0 && f.n[x] > 0;
-        
-#pragma unroll
-        for (int x = 0; x < 2 && ok; ++x) {
-          if (!act[x]) continue;
-          ok = FPB_TW(3, mbar_wait(q_full + x, qc[x] & 1, abort) && mbar_wait(o_empty + x, (oc[x] & 1) ^ 1, abort));
-          ++qc[x];
-          ++oc[x];
-        }
-        for (int x = 0; x < 2 && ok; ++x)
-          if (act[x]) ok = issue_s(x);
-        const int nmax = max(f.n[0], f.n[1]);
-        for (int j = 0; j < nmax && ok; ++j) {
-          
-#pragma unroll
-        for (int x = 0; x < 2 && ok; ++x) {
-            if (j >= f.n[x]) continue;
-            if (!FPB_TW(0, mbar_wait(p_full + x, pc[x] & 1, abort))) { ok = false; break; }
-            ++pc[x];
-            const int sl = vc & 1;
-            if (!FPB_TW(2, mbar_wait(v_full + sl, (vc >> 1) & 1, abort))) { ok = false; break; }
-            ++vc;
+        if (st[x] == kNeedS) {
+          const bool q_ok = jj[x] > 0 || mbar_probe(q_full + x, qc[x] & 1);
+          why[x] = q_ok ? 1 : 3;
+          if (q_ok && mbar_probe(k_full + x, kc[x] & 1)) {
+            if (jj[x] == 0) ++qc[x];
+            ++kc[x];
             tc_fence_after();
-            const uint32_t v_base = smem_u32(sV + sl * kAttnTile);
+            const uint32_t q_base = smem_u32(smem + x * 3 * kAttnTile);
+            const uint32_t k_base = q_base + kAttnTile;
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+              const uint32_t off = (ks >> 2) * kAttnHalf + (ks & 3) * 32;
+              umma_ss(tmem + x * 128, sdesc_sw128(q_base + off, 16, 1024), sdesc_sw128(k_base + off, 16, 1024),
+                      id_s, ks > 0);
+            }
+            umma_commit(k_empty + x);
+            umma_commit(s_full + x);
+            st[x] = kNeedPV;
+            progress = true;
+          }
+        }
+        if (st[x] == kNeedPV) {
+          const bool o_ok = jj[x] > 0 || mbar_probe(o_empty + x, (oc[x] & 1) ^ 1);
+          const bool p_ok = o_ok && mbar_probe(p_full + x, pc[x] & 1);
+          why[x] = !o_ok ? 3 : (!p_ok ? 0 : 2);
+          if (p_ok && mbar_probe(v_full + x, vc[x] & 1)) {
+            if (jj[x] == 0) ++oc[x];
+            ++pc[x];
+            ++vc[x];
+            tc_fence_after();
+            const uint32_t v_base = smem_u32(smem + x * 3 * kAttnTile + 2 * kAttnTile);
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
               // A = P (TMEM, 16-bit pairs: 8 columns per 16 keys); B = V rows ks*16.. (MN-major)
               umma_ts(tmem + 256 + x * 128, tmem + x * 128 + ks * 8,
-                      sdesc_sw128(v_base + ks * 2048, kAttnHalf, 1024), id_o, (j > 0 || ks > 0) ? 1u : 0u);
+                      sdesc_sw128(v_base + ks * 2048, kAttnHalf, 1024), id_o, (jj[x] > 0 || ks > 0) ? 1u : 0u);
             }
-            umma_commit(v_empty + sl);
-            if (j == f.n[x] - 1) umma_commit(o_full + x);
-            else ok = issue_s(x);
+            umma_commit(v_empty + x);
+            if (jj[x] == nn[x] - 1) {
+              umma_commit(o_full + x);
+              st[x] = kNeedItem;
+            } else {
+              ++jj[x];
+              st[x] = kNeedS;
+            }
+            progress = true;
           }
         }
       }
-      umma_commit(mma_done);
-      volatile int no_abort = 0;
-      mbar_wait(mma_done, 0, &no_abort);
+      if (progress) {
+        last_progress = global_timer_ns();
+      } else if (*abort || global_timer_ns() - last_progress > kWaitLimitNs) {
+        *abort = 1;
+        break;
+      }
     }
+    umma_commit(mma_done);
+    volatile int no_abort = 0;
+    mbar_wait(mma_done, 0, &no_abort);
   }
   } else {
     regs_inc<kAttnSoftmaxRegs>();
-    // ------------------------------------------------------------ softmax + epilogue
-    const int x = (warp - 4) >> 2;     // tile
+    // ------------------------------------------------------------ softmax + epilogue of pipeline x
+    const int x = (warp - 4) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;    // query row within the block (= TMEM lane)
-    const int et = r;                  // thread index within the tile's warpgroup
+    const int et = r;                  // thread index within the pipeline's warpgroup
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const uint32_t t_s = tmem + x * 128 + lane_off;
     const uint32_t t_o = tmem + 256 + x * 128 + lane_off;
-    uint8_t* stage = sQ + x * kAttnTile;
+    uint8_t* stage = smem + x * 3 * kAttnTile;  // the pipeline's Q tile, free once O is final
     const float c = A.c;
     uint32_t it = 0, sc = 0, oc = 0, ep = 0;
-    auto group_sync = [&]() -> bool {  // all 128 threads of this tile, bounded
+    auto group_sync = [&]() -> bool {  // all 128 threads of this pipeline, bounded
       mbar_arrive(epi + x);
       return FPB_TW(12, mbar_wait_warp(epi + x, (ep++) & 1, abort));
     };
     while (true) {
       const int slot = it & 1;
-      if (!FPB_TW(7, mbar_wait_warp(item_full + slot, (it >> 1) & 1, abort))) break;
-      const ItemInfo f = ring[slot];
-      mbar_arrive(item_empty + slot);
+      if (!FPB_TW(7, mbar_wait_warp(item_full + 2 * x + slot, (it >> 1) & 1, abort))) break;
+      const ItemInfo f = ring[2 * x + slot];
+      mbar_arrive(item_empty + 2 * x + slot);
       ++it;
       if (f.valid == 0) break;
       if (f.valid == 2) continue;
-      const int hx = x ? f.h[1] : f.h[0];
-      if (hx < 0) continue;
-      const int n = x ? f.n[1] : f.n[0];
+      const int hx = f.h;
+      const int n = f.n;
       const int vr = min(kBlock, f.len - f.qb * kBlock);
       T* orow = reinterpret_cast<T*>(A.out) + (int64_t)f.bcoord * A.o_sb +
                 (int64_t)(f.start + f.qb * kBlock) * A.o_ss + (int64_t)hx * A.o_sh;
@@ -397,9 +362,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         continue;
       }
       // lists are ascending and causal, so only the last entry can be the diagonal block
-      int last_kb = __ldg(list_of(f, hx) + n - 1);
-      if (last_kb < 0 || last_kb > f.qb) last_kb = f.qb;
-      const bool last_is_diag = last_kb == f.qb;
+      const bool last_is_diag = f.last_kb == f.qb || f.last_kb < 0 || f.last_kb > f.qb;
       float m_use = -INFINITY, l = 0.f;
       bool ok = true;
       for (int j = 0; j < n; ++j) {
