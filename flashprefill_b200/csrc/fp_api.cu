@@ -12,6 +12,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 #include <string>
 
 #include "../../include/flashprefill_b200.h"
@@ -277,6 +278,12 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
   A.o_ss = os[1];
   A.o_sh = os[2];
   A.profile = std::getenv("FLASHPREFILL_B200_PROFILE") != nullptr;
+  A.alt_issue = std::getenv("FLASHPREFILL_B200_ISSUE") && std::strcmp(std::getenv("FLASHPREFILL_B200_ISSUE"), "alt") == 0;
+  A.trace = std::getenv("FLASHPREFILL_B200_TRACE") != nullptr;
+  if (A.trace) {
+    static const unsigned int zero = 0;
+    FPB_CUDA(cudaMemcpyToSymbolAsync(g_attn_trace_n, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, stream));
+  }
   if (A.profile) {
     static const unsigned long long zeros[kProfSlots] = {};
     FPB_CUDA(cudaMemcpyToSymbolAsync(g_attn_prof, zeros, sizeof(zeros), 0, cudaMemcpyHostToDevice, stream));
@@ -301,15 +308,27 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
     sparse_attn_kernel<__half><<<grid, kAttnThreads, smem, stream>>>(tm_q, tm_k, tm_v, tm_o, A);
   }
   FPB_CUDA(cudaGetLastError());
+  if (A.trace) {  // debug: CTA 0's event trace, written to the file the variable names
+    unsigned int n = 0;
+    FPB_CUDA(cudaMemcpyFromSymbolAsync(&n, g_attn_trace_n, sizeof(n), 0, cudaMemcpyDeviceToHost, stream));
+    FPB_CUDA(cudaStreamSynchronize(stream));
+    n = std::min(n, (unsigned)kTraceCap);
+    std::vector<unsigned long long> buf(2 * (size_t)n + 1);
+    FPB_CUDA(cudaMemcpyFromSymbol(buf.data(), g_attn_trace, 16 * (size_t)n));
+    if (FILE* fh = std::fopen(std::getenv("FLASHPREFILL_B200_TRACE"), "wb")) {
+      std::fwrite(buf.data(), 16, n, fh);
+      std::fclose(fh);
+    }
+  }
   if (A.profile) {  // debug instrumentation: synchronises and prints per-phase cycle sums
     unsigned long long h[kProfSlots];
     FPB_CUDA(cudaMemcpyFromSymbolAsync(h, g_attn_prof, sizeof(h), 0, cudaMemcpyDeviceToHost, stream));
     FPB_CUDA(cudaStreamSynchronize(stream));
     static const char* names[kProfSlots] = {
-        "mma_blk_p_full", "mma_blk_k_full", "mma_blk_v_full", "mma_blk_q_or_o", "mma_blk_item_or_issue",
+        "mma_blk_p_full", "mma_blk_k_full", "mma_blk_v_full", "mma_blk_q_or_o", "mma_wait_item",
         "sm_wait_s_full", "sm_wait_o_full", "sm_wait_item", "sm_pass1", "sm_rescale", "sm_pass2", "sm_epilogue",
         "sm_epi_sync", "prod_wait_k_empty", "prod_wait_q_empty", "prod_wait_item_empty", "prod_wait_v_empty", "mma_pipe_done",
-        "cta_total_cycles", "items", "softmax_block_iters", "rescales", "sm_tmem_ld_S", "sm_tmem_st_P_wait"};
+        "cta_total_cycles", "items", "softmax_block_iters", "rescales", "sm_tmem_ld_S", "sm_tmem_st_P_wait", "sm_wait_rowmax"};
     fprintf(stderr, "[fpb profile] grid=%u\n", grid);
     for (int i = 0; i < kProfSlots; ++i) fprintf(stderr, "[fpb profile] %-26s %llu\n", names[i], h[i]);
   }

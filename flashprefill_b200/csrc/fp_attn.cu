@@ -35,26 +35,29 @@ struct AttnArgs {
   const int32_t* cnt;        // [hq][tiles_ub]
   int* counter;              // work-item counter, zero at launch
   int profile;               // accumulate g_attn_prof
+  int trace;                 // record g_attn_trace for CTA 0
+  int alt_issue;             // one MMA issuer alternating between the pipelines (else one per pipeline)
   int total_items;           // tiles_ub * hq
   void* out;                 // output base (masked-store path)
   int64_t o_sb, o_ss, o_sh;  // output strides in elements
 };
 
-constexpr int kAttnThreads = 384;
+constexpr int kAttnThreads = 640;
 #ifndef FPB_SOFTMAX_PROBE
 #define FPB_SOFTMAX_PROBE 0
 #endif
 constexpr bool kSoftmaxProbe = FPB_SOFTMAX_PROBE;
-// Register split (per thread): the kernel is compiled for 168 (= 65536 / 384, rounded down
-// to a multiple of 8); role warps 0-3 give back to 80 and the two softmax warpgroups grow
-// to 208: 128*80 + 256*208 = 63488 <= 384*168 = 64512.  The host refuses to launch unless the compiled
-// register count is exactly kAttnLaunchRegs.
-constexpr int kAttnLaunchRegs = 168, kAttnRoleRegs = 80, kAttnSoftmaxRegs = 208;
-static_assert(128 * kAttnRoleRegs + 256 * kAttnSoftmaxRegs <= kAttnThreads * kAttnLaunchRegs, "register split");
+
+// Register split (per thread): the kernel is compiled for 96 (= 65536 / 640, rounded down
+// to a multiple of 8); role warps 0-3 give back to 64 and the four softmax warpgroups grow
+// to 104: 128*64 + 512*104 = 61440 <= 640*96 = 61440.  The host refuses to launch unless
+// the compiled register count is exactly kAttnLaunchRegs.
+constexpr int kAttnLaunchRegs = 96, kAttnRoleRegs = 64, kAttnSoftmaxRegs = 104;
+static_assert(128 * kAttnRoleRegs + 512 * kAttnSoftmaxRegs <= kAttnThreads * kAttnLaunchRegs, "register split");
 
 // Opt-in instrumentation (FLASHPREFILL_B200_PROFILE=1): cycles spent per wait / phase,
 // summed over CTAs.  Indices: see kProfNames in fp_api.cu.
-constexpr int kProfSlots = 24;
+constexpr int kProfSlots = 25;
 __device__ unsigned long long g_attn_prof[kProfSlots];
 struct ProfAcc {  // counters live in shared memory, flushed once per CTA
   unsigned long long* sm;
@@ -63,6 +66,20 @@ struct ProfAcc {  // counters live in shared memory, flushed once per CTA
   }
 };
 __device__ __forceinline__ unsigned long long clk() { return clock64(); }
+// Opt-in event trace of CTA 0: (clock, kind << 56 | a << 28 | b) pairs.
+constexpr int kTraceCap = 1 << 16;
+__device__ unsigned long long g_attn_trace[2 * kTraceCap];
+__device__ unsigned int g_attn_trace_n;
+#define trace(on, kind, a, b) trace_((on), trace_ctr, (kind), (a), (b))
+__device__ __forceinline__ void trace_(bool on, unsigned* ctr, uint32_t kind, uint32_t a, uint32_t b) {
+  if (!on) return;
+  const unsigned long long now = clock64();
+  const unsigned i = atomicAdd(ctr, 1u);  // shared-memory counter: short round trip
+  if (i < kTraceCap) {
+    g_attn_trace[2 * i] = now;
+    g_attn_trace[2 * i + 1] = ((unsigned long long)kind << 56) | ((unsigned long long)a << 28) | b;
+  }
+}
 #define FPB_TW(slot, call)                   \
   ({                                         \
     const unsigned long long t0_ = clk();    \
@@ -73,7 +90,8 @@ __device__ __forceinline__ unsigned long long clk() { return clock64(); }
 constexpr uint32_t kAttnTile = 128 * 128 * 2;
 constexpr uint32_t kAttnHalf = kAttnTile / 2;
 
-__host__ __device__ constexpr size_t attn_smem_bytes() { return (size_t)kAttnTile * 6 + 1024 + 1024; }
+// 6 tiles, alignment slack, barriers / item ring / counters, row max and sum exchange (6 KB)
+__host__ __device__ constexpr size_t attn_smem_bytes() { return (size_t)kAttnTile * 6 + 1024 + 1024 + 6144; }
 
 // One work item as published by a pipeline's scheduler in its smem ring.
 struct ItemInfo {
@@ -104,17 +122,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* o_full = bars + 24;
   uint64_t* o_empty = bars + 26;
   uint64_t* epi = bars + 28;         // bounded sync of a pipeline's 128 epilogue threads
-  uint64_t* mma_done = bars + 30;
-  ItemInfo* ring = reinterpret_cast<ItemInfo*>(bars + 32);  // [pipeline][slot]
+  uint64_t* mma_done = bars + 30;   // [pipeline]
+  uint64_t* mx_bar = bars + 32;      // [pipeline] row-max exchange of the two halves
+  uint64_t* stage_free = bars + 34;  // [pipeline] epilogue done with the V tile (output staging)
+  ItemInfo* ring = reinterpret_cast<ItemInfo*>(bars + 40);  // [pipeline][slot]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring + 4);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  unsigned* trace_ctr = tmem_slot + 3;
   unsigned long long* prof_smem = reinterpret_cast<unsigned long long*>(tmem_slot + 4);  // [kProfSlots]
+  float* xchg = reinterpret_cast<float*>(smem + 6 * kAttnTile + 1024);  // 1536 floats
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < 4; ++i) {
       mbar_init(item_full + i, 1);
-      mbar_init(item_empty + i, 1 + 128);
+      mbar_init(item_empty + i, 1 + 256);
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(q_full + x, 1);
@@ -124,13 +146,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(v_full + x, 1);
       mbar_init(v_empty + x, 1);
       mbar_init(s_full + x, 1);
-      mbar_init(p_full + x, 128);
+      mbar_init(p_full + x, 256);
       mbar_init(o_full + x, 1);
-      mbar_init(o_empty + x, 128);
-      mbar_init(epi + x, 128);
+      mbar_init(o_empty + x, 256);
+      mbar_init(epi + x, 256);
+      mbar_init(mx_bar + x, 256);
+      mbar_init(stage_free + x, 1);
     }
     mbar_init(mma_done, 1);
+    mbar_init(mma_done + 1, 1);
     *abort = 0;
+    *trace_ctr = 0;
     for (int i = 0; i < kProfSlots; ++i) prof_smem[i] = 0;
     fence_mbar_init();
   }
@@ -147,6 +173,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   pa.sm = (A.profile && (threadIdx.x < 128 ? lane == 0 : (threadIdx.x & 127) == 0)) ? prof_smem : nullptr;
   const unsigned long long t_kernel0 = clk();
   const int group = A.P.hq / A.P.hk;
+  const bool tr = A.trace && blockIdx.x == 0;
 
   if (warp < 4) {
   regs_dec<kAttnRoleRegs>();
@@ -160,11 +187,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
     const uint64_t stream_once = l2_policy_evict_first();
-    uint32_t it = 0, kseq = 0, vseq = 0, qld = 0;
+    uint32_t it = 0, kseq = 0, vseq = 0, qld = 0, sfc = 0;
     bool ok = true;
     while (ok) {
       const int slot = it & 1;
-      if (!FPB_TW(15, mbar_wait(item_empty + 2 * x + slot, ((it >> 1) & 1) ^ 1, abort))) break;
+      if (!FPB_TW(15, mbar_wait_sleep(item_empty + 2 * x + slot, ((it >> 1) & 1) ^ 1, abort))) break;
       ItemInfo f{};
       const int id = atomicAdd(A.counter, 1);
       const int32_t* lst = nullptr;
@@ -173,7 +200,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       } else {
         SeqInfo s;
         int qb;
-        if (!decode_item(A.P, id / A.P.hq, s, qb)) {
+        const int tile = id / A.P.hq, h = id - tile * A.P.hq;
+        if (!decode_item(A.P, tile, s, qb)) {
           f.valid = 2;
         } else {
           f.valid = 1;
@@ -182,7 +210,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           f.tile_base = s.tile_base;
           f.bcoord = s.bcoord;
           f.qb = qb;
-          f.h = id % A.P.hq;
+          f.h = h;
           const int64_t row = (int64_t)f.h * A.P.tiles_ub + s.tile_base + qb;
           f.n = max(0, min(__ldg(A.cnt + row), qb + 1));
           lst = A.idx + row * A.P.cap;
@@ -196,7 +224,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (f.valid == 0) break;
       if (f.valid == 2 || f.n == 0) continue;
       const int hk = f.h / group;
-      if (!FPB_TW(14, mbar_wait(q_empty + x, (qld & 1) ^ 1, abort))) break;
+      if (!FPB_TW(14, mbar_wait_sleep(q_empty + x, (qld & 1) ^ 1, abort))) break;
       ++qld;
       const int qrow = f.start + f.qb * kBlock;
       mbar_arrive_expect_tx(q_full + x, kAttnTile);
@@ -209,12 +237,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           kb = f.qb;
         }
         const int krow = f.start + kb * kBlock;
-        if (!FPB_TW(13, mbar_wait(k_empty + x, (kseq & 1) ^ 1, abort))) { ok = false; break; }
+        if (!FPB_TW(13, mbar_wait_sleep(k_empty + x, (kseq & 1) ^ 1, abort))) { ok = false; break; }
+        trace(tr, 1, x, kseq);
         ++kseq;
         mbar_arrive_expect_tx(k_full + x, kAttnTile);
         tma_load_4d(sK, &tm_k, k_full + x, 0, hk, krow, f.bcoord);
         tma_load_4d(sK + kAttnHalf, &tm_k, k_full + x, 64, hk, krow, f.bcoord);
-        if (!FPB_TW(16, mbar_wait(v_empty + x, (vseq & 1) ^ 1, abort))) { ok = false; break; }
+        if (!FPB_TW(16, mbar_wait_sleep(v_empty + x, (vseq & 1) ^ 1, abort))) { ok = false; break; }
+        if (j == 0 && qld > 1) {  // the previous item's epilogue stages its output in the V tile
+          if (!FPB_TW(16, mbar_wait_sleep(stage_free + x, sfc & 1, abort))) { ok = false; break; }
+          ++sfc;
+        }
+        trace(tr, 2, x, vseq);
         ++vseq;
         mbar_arrive_expect_tx(v_full + x, kAttnTile);
         tma_load_4d(sV, &tm_v, v_full + x, 0, hk, krow, f.bcoord);
@@ -227,27 +261,68 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (vseq) mbar_wait(v_full + x, (vseq - 1) & 1, &no_abort);
       if (qld) mbar_wait(q_full + x, (qld - 1) & 1, &no_abort);
     }
-  } else if (warp == 1 && lane == 0) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (A.alt_issue && warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (both pipelines)
+    // PV_x(j) and S_x(j+1) are issued back to back, and the pipelines take turns: while the
+    // tensor core works for one pipeline, the other one's softmax runs.  A pipeline whose
+    // turn it is but that waits for loads or an item (not for its softmax) lets the other go.
     constexpr uint32_t id_s = idesc_f16(128, 128, DT<T>::is_bf16, false);
     constexpr uint32_t id_o = idesc_f16(128, 128, DT<T>::is_bf16, true);
     enum { kNeedItem = 0, kNeedS = 1, kNeedPV = 2, kDone = 3 };
     int st[2] = {kNeedItem, kNeedItem}, jj[2] = {0, 0}, nn[2] = {0, 0};
     uint32_t it[2] = {0, 0}, qc[2] = {0, 0}, kc[2] = {0, 0}, vc[2] = {0, 0}, pc[2] = {0, 0}, oc[2] = {0, 0};
+    int turn = 0;
     uint64_t last_progress = global_timer_ns();
-    int why[2] = {4, 4};  // profile: reason each pipeline was blocked in the previous sweep
-    unsigned long long t_prev = clk();
+    auto try_s = [&](int x) -> bool {
+      if (st[x] != kNeedS) return false;
+      if (!(jj[x] > 0 || mbar_probe(q_full + x, qc[x] & 1))) return false;
+      if (!mbar_probe(k_full + x, kc[x] & 1)) return false;
+      if (jj[x] == 0) ++qc[x];
+      ++kc[x];
+      tc_fence_after();
+      const uint32_t q_base = smem_u32(smem + x * 3 * kAttnTile);
+      const uint32_t k_base = q_base + kAttnTile;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t off = (ks >> 2) * kAttnHalf + (ks & 3) * 32;
+        umma_ss(tmem + x * 128, sdesc_sw128(q_base + off, 16, 1024), sdesc_sw128(k_base + off, 16, 1024), id_s,
+                ks > 0);
+      }
+      umma_commit(k_empty + x);
+      umma_commit(s_full + x);
+      if (jj[x] == nn[x] - 1) umma_commit(q_empty + x);  // the item's last read of Q
+      trace(tr, 3, x, kc[x]);
+      st[x] = kNeedPV;
+      return true;
+    };
+    auto pv_ready = [&](int x) -> bool {
+      return st[x] == kNeedPV && (jj[x] > 0 || mbar_probe(o_empty + x, (oc[x] & 1) ^ 1)) &&
+             mbar_probe(p_full + x, pc[x] & 1) && mbar_probe(v_full + x, vc[x] & 1);
+    };
+    auto issue_pv = [&](int x) {
+      if (jj[x] == 0) ++oc[x];
+      ++pc[x];
+      ++vc[x];
+      tc_fence_after();
+      const uint32_t v_base = smem_u32(smem + x * 3 * kAttnTile + 2 * kAttnTile);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma_ts(tmem + 256 + x * 128, tmem + x * 128 + ks * 8, sdesc_sw128(v_base + ks * 2048, kAttnHalf, 1024),
+                id_o, (jj[x] > 0 || ks > 0) ? 1u : 0u);
+      umma_commit(v_empty + x);
+      trace(tr, 4, x, pc[x]);
+      if (jj[x] == nn[x] - 1) {
+        umma_commit(o_full + x);
+        st[x] = kNeedItem;
+      } else {
+        ++jj[x];
+        st[x] = kNeedS;
+      }
+    };
     while (st[0] != kDone || st[1] != kDone) {
       bool progress = false;
-      if (pa.sm) {
-        const unsigned long long now = clk();
-        pa.add(why[0], now - t_prev);
-        pa.add(why[1], now - t_prev);
-        t_prev = now;
-      }
 #pragma unroll
       for (int x = 0; x < 2; ++x) {
-        why[x] = st[x] == kDone ? 17 : 4;
         if (st[x] == kNeedItem) {
           const int slot = it[x] & 1;
           if (mbar_probe(item_full + 2 * x + slot, (it[x] >> 1) & 1)) {
@@ -255,62 +330,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             mbar_arrive(item_empty + 2 * x + slot);
             ++it[x];
             progress = true;
-            if (f.valid == 0) st[x] = kDone;
-            else if (f.valid == 1 && f.n > 0) {
+            if (f.valid == 0) {
+              st[x] = kDone;
+            } else if (f.valid == 1 && f.n > 0) {
               st[x] = kNeedS;
               jj[x] = 0;
               nn[x] = f.n;
             }
           }
         }
-        if (st[x] == kNeedS) {
-          const bool q_ok = jj[x] > 0 || mbar_probe(q_full + x, qc[x] & 1);
-          why[x] = q_ok ? 1 : 3;
-          if (q_ok && mbar_probe(k_full + x, kc[x] & 1)) {
-            if (jj[x] == 0) ++qc[x];
-            ++kc[x];
-            tc_fence_after();
-            const uint32_t q_base = smem_u32(smem + x * 3 * kAttnTile);
-            const uint32_t k_base = q_base + kAttnTile;
-#pragma unroll
-            for (int ks = 0; ks < 8; ++ks) {
-              const uint32_t off = (ks >> 2) * kAttnHalf + (ks & 3) * 32;
-              umma_ss(tmem + x * 128, sdesc_sw128(q_base + off, 16, 1024), sdesc_sw128(k_base + off, 16, 1024),
-                      id_s, ks > 0);
-            }
-            umma_commit(k_empty + x);
-            umma_commit(s_full + x);
-            st[x] = kNeedPV;
-            progress = true;
-          }
-        }
-        if (st[x] == kNeedPV) {
-          const bool o_ok = jj[x] > 0 || mbar_probe(o_empty + x, (oc[x] & 1) ^ 1);
-          const bool p_ok = o_ok && mbar_probe(p_full + x, pc[x] & 1);
-          why[x] = !o_ok ? 3 : (!p_ok ? 0 : 2);
-          if (p_ok && mbar_probe(v_full + x, vc[x] & 1)) {
-            if (jj[x] == 0) ++oc[x];
-            ++pc[x];
-            ++vc[x];
-            tc_fence_after();
-            const uint32_t v_base = smem_u32(smem + x * 3 * kAttnTile + 2 * kAttnTile);
-#pragma unroll
-            for (int ks = 0; ks < 8; ++ks) {
-              // A = P (TMEM, 16-bit pairs: 8 columns per 16 keys); B = V rows ks*16.. (MN-major)
-              umma_ts(tmem + 256 + x * 128, tmem + x * 128 + ks * 8,
-                      sdesc_sw128(v_base + ks * 2048, kAttnHalf, 1024), id_o, (jj[x] > 0 || ks > 0) ? 1u : 0u);
-            }
-            umma_commit(v_empty + x);
-            if (jj[x] == nn[x] - 1) {
-              umma_commit(o_full + x);
-              st[x] = kNeedItem;
-            } else {
-              ++jj[x];
-              st[x] = kNeedS;
-            }
-            progress = true;
-          }
-        }
+        if (try_s(x)) progress = true;
+      }
+      const int y = turn, z = turn ^ 1;
+      if (pv_ready(y)) {
+        issue_pv(y);
+        try_s(y);
+        turn = z;
+        progress = true;
+      } else if (st[y] != kNeedPV && pv_ready(z)) {
+        issue_pv(z);
+        try_s(z);
+        progress = true;
       }
       if (progress) {
         last_progress = global_timer_ns();
@@ -322,27 +362,94 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     umma_commit(mma_done);
     volatile int no_abort = 0;
     mbar_wait(mma_done, 0, &no_abort);
+  } else if (!A.alt_issue && (warp == 1 || warp == 3) && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer of pipeline x
+    // One issuing thread per pipeline: tcgen05.mma issue stalls while the tensor core's
+    // instruction queue is full (about one group of eight), so an issuer shared by both
+    // pipelines would hold one pipeline's ready MMAs behind the other's.
+    const int x = warp >> 1;
+    constexpr uint32_t id_s = idesc_f16(128, 128, DT<T>::is_bf16, false);
+    constexpr uint32_t id_o = idesc_f16(128, 128, DT<T>::is_bf16, true);
+    const uint32_t q_base = smem_u32(smem + x * 3 * kAttnTile);
+    const uint32_t k_base = q_base + kAttnTile, v_base = q_base + 2 * kAttnTile;
+    const uint32_t t_s = tmem + x * 128, t_o = tmem + 256 + x * 128;
+    uint32_t it = 0, qc = 0, kc = 0, vc = 0, pc = 0, oc = 0;
+    bool ok = true;
+    while (ok) {
+      const int slot = it & 1;
+      if (!FPB_TW(4, mbar_wait_sleep(item_full + 2 * x + slot, (it >> 1) & 1, abort))) break;
+      const ItemInfo f = ring[2 * x + slot];
+      mbar_arrive(item_empty + 2 * x + slot);
+      ++it;
+      if (f.valid == 0) break;
+      if (f.valid != 1 || f.n == 0) continue;
+      for (int j = 0; j < f.n; ++j) {
+        if (j == 0) {
+          if (!FPB_TW(3, mbar_wait_sleep(q_full + x, qc & 1, abort))) { ok = false; break; }
+          ++qc;
+        }
+        if (!FPB_TW(1, mbar_wait_sleep(k_full + x, kc & 1, abort))) { ok = false; break; }
+        ++kc;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t off = (ks >> 2) * kAttnHalf + (ks & 3) * 32;
+          umma_ss(t_s, sdesc_sw128(q_base + off, 16, 1024), sdesc_sw128(k_base + off, 16, 1024), id_s, ks > 0);
+        }
+        umma_commit(k_empty + x);
+        umma_commit(s_full + x);
+        if (j == f.n - 1) umma_commit(q_empty + x);  // the item's last read of Q
+        trace(tr, 3, x, kc);
+        if (j == 0) {  // the previous item's epilogue must have read O
+          if (!FPB_TW(3, mbar_wait_sleep(o_empty + x, (oc & 1) ^ 1, abort))) { ok = false; break; }
+          ++oc;
+        }
+        if (!FPB_TW(0, mbar_wait_sleep(p_full + x, pc & 1, abort))) { ok = false; break; }
+        ++pc;
+        if (!FPB_TW(2, mbar_wait_sleep(v_full + x, vc & 1, abort))) { ok = false; break; }
+        ++vc;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          // A = P (TMEM, 16-bit pairs: 8 columns per 16 keys); B = V rows ks*16.. (MN-major)
+          umma_ts(t_o, t_s + ks * 8, sdesc_sw128(v_base + ks * 2048, kAttnHalf, 1024), id_o,
+                  (j > 0 || ks > 0) ? 1u : 0u);
+        }
+        umma_commit(v_empty + x);
+        trace(tr, 4, x, pc);
+        if (j == f.n - 1) umma_commit(o_full + x);
+      }
+    }
+    umma_commit(mma_done + x);
+    volatile int no_abort = 0;
+    mbar_wait(mma_done + x, 0, &no_abort);
   }
   } else {
     regs_inc<kAttnSoftmaxRegs>();
     // ------------------------------------------------------------ softmax + epilogue of pipeline x
-    const int x = (warp - 4) >> 2;
+    // Two warpgroups per pipeline: thread (hh, r) owns columns [64*hh, 64*hh + 64) of query
+    // row r in S, P and O.  The two halves of a row agree on its running max through shared
+    // memory once per block (mx_bar); each keeps its own partial row sum.
+    const int w = warp - 4;
+    const int x = w >> 3;
+    const int hh = (w >> 2) & 1;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;    // query row within the block (= TMEM lane)
-    const int et = r;                  // thread index within the pipeline's warpgroup
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const uint32_t t_s = tmem + x * 128 + lane_off;
-    const uint32_t t_o = tmem + 256 + x * 128 + lane_off;
-    uint8_t* stage = smem + x * 3 * kAttnTile;  // the pipeline's Q tile, free once O is final
+    const uint32_t t_o = tmem + 256 + x * 128 + lane_off + hh * 64;
+    float* xch = xchg + x * 512;                // row max: [parity][half][row]
+    float* xl = xchg + 1024 + x * 256;          // row sum: [half][row]
     const float c = A.c;
-    uint32_t it = 0, sc = 0, oc = 0, ep = 0;
-    auto group_sync = [&]() -> bool {  // all 128 threads of this pipeline, bounded
+    const bool rec = tr && r == 0 && hh == 0;
+    uint32_t it = 0, sc = 0, oc = 0, ep = 0, mp = 0;
+    auto group_sync = [&]() -> bool {  // all 256 threads of this pipeline, bounded
       mbar_arrive(epi + x);
-      return FPB_TW(12, mbar_wait_warp(epi + x, (ep++) & 1, abort));
+      return FPB_TW(12, mbar_wait_warp_sleep(epi + x, (ep++) & 1, abort));
     };
     while (true) {
       const int slot = it & 1;
-      if (!FPB_TW(7, mbar_wait_warp(item_full + 2 * x + slot, (it >> 1) & 1, abort))) break;
+      if (!FPB_TW(7, mbar_wait_warp_sleep(item_full + 2 * x + slot, (it >> 1) & 1, abort))) break;
       const ItemInfo f = ring[2 * x + slot];
       mbar_arrive(item_empty + 2 * x + slot);
       ++it;
@@ -355,9 +462,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 (int64_t)(f.start + f.qb * kBlock) * A.o_ss + (int64_t)hx * A.o_sh;
       if (n == 0) {  // empty list: zeros (the reference's acc = 0, l = 1)
         if (r < vr) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + (int64_t)r * A.o_ss);
+          uint4* dst = reinterpret_cast<uint4*>(orow + (int64_t)r * A.o_ss + hh * 64);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) dst[i] = make_uint4(0, 0, 0, 0);
+          for (int i = 0; i < 8; ++i) dst[i] = make_uint4(0, 0, 0, 0);
         }
         continue;
       }
@@ -367,32 +474,36 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       bool ok = true;
       for (int j = 0; j < n; ++j) {
         const bool diag = last_is_diag && j == n - 1;
-        if (!FPB_TW(5, mbar_wait_warp<kSoftmaxProbe>(s_full + x, sc & 1, abort))) { ok = false; break; }
+        if (!FPB_TW(5, mbar_wait_warp_sleep(s_full + x, sc & 1, abort))) { ok = false; break; }
         ++sc;
         tc_fence_after();
-        // the whole 128-column row of S in registers: four loads, one wait
         const unsigned long long tp1 = clk();
+        trace(rec, 5, x, j);
         pa.add(20, 1);
-        uint32_t ua[32], ub[32], uc[32], ud[32];
-        tmem_ld32(t_s, ua);
-        tmem_ld32(t_s + 32, ub);
-        tmem_ld32(t_s + 64, uc);
-        tmem_ld32(t_s + 96, ud);
+        uint32_t ua[32], ub[32];
+        tmem_ld32(t_s + hh * 64, ua);
+        tmem_ld32(t_s + hh * 64 + 32, ub);
         tmem_ld_wait();
         pa.add(22, clk() - tp1);
-#define FPB_U(i) ((i) < 32 ? ua[(i)] : (i) < 64 ? ub[(i) - 32] : (i) < 96 ? uc[(i) - 64] : ud[(i) - 96])
+#define FPB_U(i) ((i) < 32 ? ua[(i)] : ub[(i) - 32])
         if (diag) {  // only the diagonal block needs the causal mask
 #pragma unroll
-          for (int i = 0; i < 128; ++i)
-            if (i > r) FPB_U(i) = __float_as_uint(-INFINITY);
+          for (int i = 0; i < 64; ++i)
+            if (hh * 64 + i > r) FPB_U(i) = __float_as_uint(-INFINITY);
         }
         float mx = -INFINITY, m1 = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 128; i += 4) {
+        for (int i = 0; i < 64; i += 4) {
           mx = max3(mx, __uint_as_float(FPB_U(i)), __uint_as_float(FPB_U(i + 1)));
           m1 = max3(m1, __uint_as_float(FPB_U(i + 2)), __uint_as_float(FPB_U(i + 3)));
         }
         mx = fmaxf(mx, m1);
+        // exchange with the other half of the row (double-buffered by block parity)
+        xch[(mp & 1) * 256 + hh * 128 + r] = mx;
+        mbar_arrive(mx_bar + x);
+        if (!FPB_TW(24, mbar_wait_warp_sleep(mx_bar + x, mp & 1, abort))) { ok = false; break; }
+        mx = fmaxf(mx, xch[(mp & 1) * 256 + (hh ^ 1) * 128 + r]);
+        ++mp;
         const float m_blk = mx * c;
         float scale_o = 1.f;
         if (j == 0) {
@@ -404,12 +515,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         const unsigned long long tp3 = clk();
         pa.add(8, tp3 - tp1);
-        // P = exp2(s*c - m), written as 16-bit pairs over S columns [0, 64); one pair in
-        // four is evaluated on the FMA pipe (exp2_poly2), the rest by ex2.approx.
+        // P = exp2(s*c - m) as 16-bit pairs over S columns [32*hh, 32*hh + 32) (the S values
+        // there, the other half's, were read before the exchange above); one pair in four
+        // is evaluated on the FMA pipe (exp2_poly2), the rest by ex2.approx.
         const float neg_m = -m_use;
         float rs = 0.f, rs1 = 0.f;
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
+        for (int ch = 0; ch < 2; ++ch) {
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
@@ -425,30 +537,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             add2(rs, rs1, rs, rs1, p0, p1);
             pk[i >> 1] = DT<T>::pack(p0, p1);
           }
-          tmem_st16(t_s + ch * 16, pk);
+          tmem_st16(t_s + hh * 32 + ch * 16, pk);
         }
 #undef FPB_U
         const unsigned long long tst = clk();
         pa.add(10, tst - tp3);
         rs += rs1;
         if (__any_sync(0xffffffffu, scale_o != 1.f)) {
-          // O_x holds blocks 0..j-1 (PV_x(j-1) completed before S_x(j) did); rescale it
-          // before PV_x(j) is allowed to start (p_full below)
+          // O_x holds blocks 0..j-1 (PV_x(j-1) completed before S_x(j) did); rescale this
+          // thread's 64 columns before PV_x(j) is allowed to start (p_full below)
           pa.add(21, 1);
-#pragma unroll 1
-          for (int h2 = 0; h2 < 2; ++h2) {
-            uint32_t oa[32], ob[32];
-            tmem_ld32(t_o + h2 * 64, oa);
-            tmem_ld32(t_o + h2 * 64 + 32, ob);
-            tmem_ld_wait();
+          uint32_t oa[32], ob[32];
+          tmem_ld32(t_o, oa);
+          tmem_ld32(t_o + 32, ob);
+          tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              oa[i] = __float_as_uint(__uint_as_float(oa[i]) * scale_o);
-              ob[i] = __float_as_uint(__uint_as_float(ob[i]) * scale_o);
-            }
-            tmem_st32(t_o + h2 * 64, oa);
-            tmem_st32(t_o + h2 * 64 + 32, ob);
+          for (int i = 0; i < 32; ++i) {
+            oa[i] = __float_as_uint(__uint_as_float(oa[i]) * scale_o);
+            ob[i] = __float_as_uint(__uint_as_float(ob[i]) * scale_o);
           }
+          tmem_st32(t_o, oa);
+          tmem_st32(t_o + 32, ob);
           pa.add(9, clk() - tst);
         }
         tmem_st_wait();
@@ -456,51 +565,58 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         l += rs;
         tc_fence_before();
         mbar_arrive(p_full + x);
+        trace(rec, 6, x, j);
       }
       if (!ok) break;
-      // ---- epilogue: O / l -> smem (SW128 layout, in the Q tile) -> global
-      if (!FPB_TW(6, mbar_wait_warp(o_full + x, oc & 1, abort))) break;
+      // ---- epilogue: O / l -> smem (SW128 layout, in the V tile) -> global by TMA
+      if (!FPB_TW(6, mbar_wait_warp_sleep(o_full + x, oc & 1, abort))) break;
       ++oc;
       tc_fence_after();
       const unsigned long long te0 = clk();
-      const float inv = 1.f / l;
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t u[32];
-        tmem_ld32(t_o + ch * 32, u);
-        tmem_ld_wait();
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          pk[i] = DT<T>::pack(__uint_as_float(u[2 * i]) * inv, __uint_as_float(u[2 * i + 1]) * inv);
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const int cidx = ch * 4 + q4;  // 16-byte chunk 0..15 of the row
-          uint8_t* dst = stage + (cidx >> 3) * kAttnHalf + r * 128 + (((cidx & 7) ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[q4 * 4], pk[q4 * 4 + 1], pk[q4 * 4 + 2], pk[q4 * 4 + 3]);
-        }
-      }
+      uint32_t oa[32], ob[32];
+      tmem_ld32(t_o, oa);
+      tmem_ld32(t_o + 32, ob);
+      xl[hh * 128 + r] = l;
+      tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(o_empty + x);
+      mbar_arrive(o_empty + x);  // O_x may be overwritten by the next item's first PV
+      if (!group_sync()) break;
+      const float inv = 1.f / (l + xl[(hh ^ 1) * 128 + r]);
+      uint8_t* stage = smem + x * 3 * kAttnTile + 2 * kAttnTile;  // V tile: its last PV has completed
+#pragma unroll
+      for (int q4 = 0; q4 < 8; ++q4) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int e = q4 * 8 + 2 * i;
+          const float v0 = __uint_as_float(e < 32 ? oa[e] : ob[e - 32]) * inv;
+          const float v1 = __uint_as_float(e + 1 < 32 ? oa[e + 1] : ob[e - 31]) * inv;
+          pk[i] = DT<T>::pack(v0, v1);
+        }
+        uint8_t* dst = stage + hh * kAttnHalf + r * 128 + ((q4 ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
       fence_proxy_async_smem();
       if (!group_sync()) break;
+      const int et = hh * 128 + r;
       if (vr == kBlock) {
         if (et == 0) {
           const int qrow = f.start + f.qb * kBlock;
-          tma_store_4d(&tm_o, stage, 0, hx, qrow, f.bcoord);
-          tma_store_4d(&tm_o, stage + kAttnHalf, 64, hx, qrow, f.bcoord);
-          tma_store_commit_and_wait();
-          mbar_arrive(q_empty + x);
+          const uint64_t pol = l2_policy_evict_first();  // the output is not read again here
+          tma_store_4d_hint(&tm_o, stage, 0, hx, qrow, f.bcoord, pol);
+          tma_store_4d_hint(&tm_o, stage + kAttnHalf, 64, hx, qrow, f.bcoord, pol);
+          tma_store_commit_and_wait_read();
+          mbar_arrive(stage_free + x);
         }
-      } else {
-        for (int e = et; e < vr * 16; e += 128) {
+      } else {  // a sequence's last, partial block: only its rows may be written
+        for (int e = et; e < vr * 16; e += 256) {
           const int rr = e >> 4, cidx = e & 15;
           const uint4 v =
               *reinterpret_cast<const uint4*>(stage + (cidx >> 3) * kAttnHalf + rr * 128 + (((cidx & 7) ^ (rr & 7)) << 4));
           *reinterpret_cast<uint4*>(orow + (int64_t)rr * A.o_ss + cidx * 8) = v;
         }
         if (!group_sync()) break;
-        if (et == 0) mbar_arrive(q_empty + x);
+        if (et == 0) mbar_arrive(stage_free + x);
       }
       pa.add(11, clk() - te0);
     }
@@ -510,6 +626,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (A.profile && threadIdx.x < kProfSlots) atomicAdd(&g_attn_prof[threadIdx.x], prof_smem[threadIdx.x]);
+  if (tr && threadIdx.x == 0) g_attn_trace_n = *trace_ctr;
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);

@@ -17,6 +17,10 @@ namespace fpb {
 
 // A single wait never legitimately lasts longer than this; 1 s of global time.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
+#ifndef FPB_SLEEP_HINT_NS
+#define FPB_SLEEP_HINT_NS 20000
+#endif
+constexpr uint32_t kSleepHintNs = FPB_SLEEP_HINT_NS;  // suspend hint of the sleeping waits
 
 // Error bits written into the device error word (workspace offset 0).
 enum : uint32_t {
@@ -60,6 +64,17 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the phase
+// completes or about hint_ns elapses, instead of spinning on issue slots.
+__device__ __forceinline__ bool mbar_test_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 // Non-blocking probe (never suspends the thread).
 __device__ __forceinline__ bool mbar_probe(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -80,6 +95,31 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_test(bar, parity)) return true;
     if (*abort) return false;
     if (global_timer_ns() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
+// Bounded wait that sleeps between polls (for waits that are usually long).
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (mbar_test_sleep(bar, parity, kSleepHintNs)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    if (mbar_test_sleep(bar, parity, kSleepHintNs)) return true;
+    if (*abort) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ bool mbar_wait_warp_sleep(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    if (__all_sync(0xffffffffu, mbar_test_sleep(bar, parity, kSleepHintNs))) return true;
+    const bool stop = (*abort != 0) || (global_timer_ns() - t0 > kWaitLimitNs);
+    if (__any_sync(0xffffffffu, stop)) {
       *abort = 1;
       return false;
     }
@@ -134,6 +174,24 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void*
   asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(map),
                "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(src))
                : "memory");
+}
+__device__ __forceinline__ void tma_store_4d_hint(const CUtensorMap* map, const void* src, int c0, int c1, int c2,
+                                                  int c3, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%1, %2, %3, %4}], [%5], %6;" ::"l"(map),
+      "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(src)), "l"(policy)
+      : "memory");
+}
+// 16-byte global store with an L2 cache policy (e.g. evict-first for streamed output).
+__device__ __forceinline__ void st_global_hint(uint4* p, uint4 v, uint64_t policy) {
+  asm volatile("st.global.L2::cache_hint.v4.u32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w), "l"(policy)
+               : "memory");
+}
+// Commit the bulk stores issued so far and wait until their shared-memory source has been read.
+__device__ __forceinline__ void tma_store_commit_and_wait_read() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 __device__ __forceinline__ void tma_store_commit_and_wait() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
