@@ -620,6 +620,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       pa.add(11, clk() - te0);
     }
+    // the epilogue waits only until its stores have read the staging tile; their global
+    // writes must be complete before the thread exits
+    tma_store_wait_all();
   }
 
   if (threadIdx.x == 0) pa.add(18, clk() - t_kernel0);

@@ -188,6 +188,8 @@ __device__ __forceinline__ void st_global_hint(uint4* p, uint4 v, uint64_t polic
                "r"(v.w), "l"(policy)
                : "memory");
 }
+// Wait until every bulk store issued by this thread has completed (global writes done).
+__device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // Commit the bulk stores issued so far and wait until their shared-memory source has been read.
 __device__ __forceinline__ void tma_store_commit_and_wait_read() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
@@ -381,6 +383,9 @@ struct DT<__nv_bfloat16> {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
   }
+  // the two values of a packed pair, widened back to fp32 (exact)
+  __device__ static __forceinline__ float lo(uint32_t p) { return __uint_as_float(p << 16); }
+  __device__ static __forceinline__ float hi(uint32_t p) { return __uint_as_float(p & 0xFFFF0000u); }
   __device__ static __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
   __device__ static __forceinline__ __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
 };
@@ -390,6 +395,10 @@ struct DT<__half> {
   __device__ static __forceinline__ uint32_t pack(float lo, float hi) {
     __half2 v = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
+  }
+  __device__ static __forceinline__ float lo(uint32_t p) { return __half2float(__ushort_as_half((unsigned short)p)); }
+  __device__ static __forceinline__ float hi(uint32_t p) {
+    return __half2float(__ushort_as_half((unsigned short)(p >> 16)));
   }
   __device__ static __forceinline__ float to_f(__half x) { return __half2float(x); }
   __device__ static __forceinline__ __half from_f(float x) { return __float2half_rn(x); }
