@@ -209,21 +209,31 @@ __global__ void __launch_bounds__(kSearchThreads, 1)
       tc_fence_after();
       const int kb = t * kBlock + lrow;
       const uint32_t taddr = tmem + acc * 128 + ((uint32_t)(quad * 32) << 16);
-      float mx = -INFINITY, s127 = 0.f;
+      // the 128 scores of this key block, kept in registers for both passes
+      uint32_t ua[32], ub[32], uc[32], ud[32];
+      tmem_ld32(taddr, ua);
+      tmem_ld32(taddr + 32, ub);
+      tmem_ld32(taddr + 64, uc);
+      tmem_ld32(taddr + 96, ud);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(acc_empty + acc);  // the accumulator may be overwritten by tile t + 2
+#define FPB_S(i) __uint_as_float((i) < 32 ? ua[(i)] : (i) < 64 ? ub[(i) - 32] : (i) < 96 ? uc[(i) - 64] : ud[(i) - 96])
+      float mx, s127;
+      if (vr == kBlock) {
+        float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t r[32];
-        tmem_ld32(taddr + ch * 32, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float v = __uint_as_float(r[i]);
-          if (ch * 32 + i < vr) mx = fmaxf(mx, v);
+        for (int i = 0; i < 128; i += 4) {
+          m0 = max3(m0, FPB_S(i), FPB_S(i + 1));
+          m1 = max3(m1, FPB_S(i + 2), FPB_S(i + 3));
         }
-        if (ch == 3) s127 = __uint_as_float(r[31]);
-      }
-      if (vr < kBlock) {
-        mx = fmaxf(mx, 0.f);   // padded rows: q = 0
+        mx = fmaxf(m0, m1);
+        s127 = FPB_S(127);
+      } else {  // a sequence's last, partial query block: padded rows have q = 0, s = 0
+        mx = 0.f;
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (i < vr) mx = fmaxf(mx, FPB_S(i));
         s127 = 0.f;
       }
       const bool causal = kb <= qb;
@@ -239,23 +249,27 @@ __global__ void __launch_bounds__(kSearchThreads, 1)
       const bool cand = causal && (m >= m_est + A.cand_off);
       float p = 0.f;
       if (__any_sync(0xffffffffu, cand && !diag)) {
+        // p = sum_r exp2(s_r c - m): one FMA per score (the reference rounds s c first; the
+        // difference is below one ulp of the exponent and only matters at the threshold)
+        const float nm = -m;
+        float p0 = 0.f, p1 = 0.f;
+        if (vr == kBlock) {
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-          uint32_t r[32];
-          tmem_ld32(taddr + ch * 32, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float sv = __fmul_rn(__uint_as_float(r[i]), c);
-            const float e = ex2_approx(__fsub_rn(sv, m));
-            if (ch * 32 + i < vr) p += e;
+          for (int i = 0; i < 128; i += 2) {
+            float x0, x1;
+            fma2(x0, x1, FPB_S(i), FPB_S(i + 1), c, c, nm, nm);
+            add2(p0, p1, p0, p1, ex2_approx(x0), ex2_approx(x1));
           }
+          p = p0 + p1;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 128; ++i)
+            if (i < vr) p += ex2_approx(__fmaf_rn(FPB_S(i), c, nm));
+          p += (float)(kBlock - vr) * ex2_approx(-m);
         }
-        if (vr < kBlock) p += (float)(kBlock - vr) * ex2_approx(-m);
       }
+#undef FPB_S
       if (diag) p = 1.f;
-      tc_fence_before();
-      mbar_arrive(acc_empty + acc);
       if (causal) {
         m_arr[kb] = m;
         p_arr[kb] = cand ? p : -1.f;
