@@ -242,6 +242,13 @@ int run_search(const Geometry& g, const void* q, const void* k, const int64_t qs
   A.normalize = g.varlen ? 0 : 1;
   A.idx = reinterpret_cast<int32_t*>(ws + L.idx);
   A.cnt = reinterpret_cast<int32_t*>(ws + L.cnt);
+  long long* dbg_t = nullptr;
+  const unsigned grid_dbg = (unsigned)L.tiles * (unsigned)g.hq;
+  if (std::getenv("FLASHPREFILL_B200_SEARCH_DBG")) {
+    FPB_CUDA(cudaMalloc(&dbg_t, sizeof(long long) * 6 * (grid_dbg / 16 + 1)));
+    FPB_CUDA(cudaMemsetAsync(dbg_t, 0, sizeof(long long) * 6 * (grid_dbg / 16 + 1), stream));
+  }
+  A.dbg_t = dbg_t;
   const unsigned grid = (unsigned)L.tiles * (unsigned)g.hq;
   if (g.dtype == FPB_BF16) {
     FPB_TRY(set_smem(block_search_kernel<__nv_bfloat16>, smem));
@@ -251,6 +258,17 @@ int run_search(const Geometry& g, const void* q, const void* k, const int64_t qs
     block_search_kernel<__half><<<grid, kSearchThreads, smem, stream>>>(tm_q, tm_mk, A);
   }
   FPB_CUDA(cudaGetLastError());
+  if (dbg_t) {
+    const size_t nrec = grid_dbg / 16 + 1;
+    std::vector<long long> h(6 * nrec);
+    FPB_CUDA(cudaMemcpyAsync(h.data(), dbg_t, sizeof(long long) * 6 * nrec, cudaMemcpyDeviceToHost, stream));
+    FPB_CUDA(cudaStreamSynchronize(stream));
+    if (FILE* fh = std::fopen(std::getenv("FLASHPREFILL_B200_SEARCH_DBG"), "wb")) {
+      std::fwrite(h.data(), sizeof(long long), h.size(), fh);
+      std::fclose(fh);
+    }
+    cudaFree(dbg_t);
+  }
   return FPB_OK;
 }
 

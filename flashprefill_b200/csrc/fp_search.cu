@@ -41,6 +41,7 @@ struct SearchArgs {
   int normalize;    // dense path: divide by (sum + 1e-9)
   int32_t* idx;     // [hq][tiles_ub][cap]
   int32_t* cnt;     // [hq][tiles_ub]
+  long long* dbg_t; // optional phase timestamps of every 16th CTA (debug)
 };
 
 constexpr int kSearchThreads = 192;
@@ -76,6 +77,7 @@ template <typename T>
 __global__ void __launch_bounds__(kSearchThreads, 1)
     block_search_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_mk,
                         const SearchArgs A) {
+  const long long t_start = clock64();
   const int hq = blockIdx.x % A.P.hq;
   SeqInfo s;
   int qb;
@@ -203,8 +205,10 @@ __global__ void __launch_bounds__(kSearchThreads, 1)
     const int vr = min(kBlock, s.len - qb * kBlock);  // valid query rows of this block
     const float c = A.c;
     bool ok = true;
+    long long t_first = 0;
     for (int t = 0; t < ntiles; ++t) {
       const int acc = t & 1;
+      if (t == 1 && et == 0) t_first = clock64();
       if (!mbar_wait_warp(acc_full + acc, (t >> 1) & 1, abort)) { ok = false; break; }
       tc_fence_after();
       const int kb = t * kBlock + lrow;
@@ -275,6 +279,7 @@ __global__ void __launch_bounds__(kSearchThreads, 1)
         p_arr[kb] = cand ? p : -1.f;
       }
     }
+    const long long t_tiles = clock64();
     // ---- normalise, threshold, compact (the failure decision is taken once for all 4 warps)
     if (!ok) *failed_flag = 1;
     named_bar_sync(1, 128);
@@ -285,30 +290,25 @@ __global__ void __launch_bounds__(kSearchThreads, 1)
       if (et == 0) *out_cnt = 0;
     } else {
       const float M = ordered_to_float(*(volatile int*)mrun);
-      float part = 0.f;
+      // pw[kb] = p[kb] * 2^(m[kb] - M).  The reference selects score >= alpha * max score with
+      // score = pw / (sum pw + 1e-9) on the dense path and score = pw on the varlen path; both
+      // are the test pw >= alpha * max pw up to the rounding of one division, which moves the
+      // decision only for scores within a few ulps of the threshold.
+      float best = 0.f;
       for (int kb = et; kb <= qb; kb += 128) {
         const float pv = p_arr[kb];
         const float pw = pv >= 0.f ? __fmul_rn(pv, ex2_approx(__fsub_rn(m_arr[kb], M))) : -1.f;
         p_arr[kb] = pw;
-        if (pw > 0.f) part += pw;
+        best = fmaxf(best, pw);
       }
-      const float denom = A.normalize ? __fadd_rn(epi_reduce_sum(part, red), 1e-9f) : 1.f;
-      float best = 0.f;
-      for (int kb = et; kb <= qb; kb += 128) {
-        const float pw = p_arr[kb];
-        if (pw >= 0.f) {
-          const float sc = A.normalize ? __fdiv_rn(pw, denom) : pw;
-          p_arr[kb] = sc;
-          best = fmaxf(best, sc);
-        }
-      }
-      const float top1 = epi_reduce_max(best, red);
-      const float thr = __fmul_rn(top1, A.alpha);
+      const float thr = __fmul_rn(epi_reduce_max(best, red), A.alpha);
       // dense min_budget: force the top-k scores in (ties -> lower block index)
       const int nwords = (qb + 1 + 31) / 32;
-      for (int wd = et; wd < nwords; wd += 128) marks[wd] = 0u;
-      named_bar_sync(1, 128);
       const int kbudget = min(A.min_budget, qb + 1);
+      if (kbudget > 0) {
+        for (int wd = et; wd < nwords; wd += 128) marks[wd] = 0u;
+        named_bar_sync(1, 128);
+      }
       for (int it = 0; it < kbudget; ++it) {
         float bv = -INFINITY;
         int bk = 0x7fffffff;
@@ -335,29 +335,37 @@ __global__ void __launch_bounds__(kSearchThreads, 1)
         }
         named_bar_sync(1, 128);
       }
-      // selection + ascending compaction, 128 blocks per round
-      int base = 0;
-      for (int k0 = 0; k0 <= qb; k0 += 128) {
-        const int kb = k0 + et;
-        bool sel = false;
-        if (kb <= qb) {
-          const float sc = p_arr[kb];
-          const bool by_score = sc >= 0.f ? (sc >= thr) : (0.f >= thr);
-          const bool forced = (marks[kb >> 5] >> (kb & 31)) & 1u;
-          sel = by_score || forced || kb < A.sink || (qb - kb) < A.window;
-        }
-        const uint32_t bal = __ballot_sync(0xffffffffu, sel);
-        const int wq = warp - 2;
-        named_bar_sync(1, 128);
-        if (lane == 0) red_i[wq] = __popc(bal);
-        named_bar_sync(1, 128);
-        int pre = base;
-        for (int j = 0; j < wq; ++j) pre += red_i[j];
-        pre += __popc(bal & ((1u << lane) - 1u));
-        if (sel) out_idx[pre] = kb;
-        base += red_i[0] + red_i[1] + red_i[2] + red_i[3];
+      // selection + ascending compaction: thread et owns the contiguous blocks
+      // [et * chunk, et * chunk + chunk); one block-wide exclusive scan of the counts
+      const int chunk = (qb + 128) / 128;  // ceil((qb + 1) / 128)
+      const int kb0 = et * chunk, kb1 = min(qb + 1, kb0 + chunk);
+      auto selected = [&](int kb) -> bool {
+        const float pw = p_arr[kb];
+        bool sel = (pw >= 0.f && pw >= thr) || kb < A.sink || (qb - kb) < A.window;
+        if (kbudget > 0) sel = sel || ((marks[kb >> 5] >> (kb & 31)) & 1u);
+        return sel;
+      };
+      int mine = 0;
+      for (int kb = kb0; kb < kb1; ++kb) mine += selected(kb);
+      int incl = mine;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
       }
+      const int wq = warp - 2;
+      if (lane == 31) red_i[wq] = incl;
+      named_bar_sync(1, 128);
+      int pre = incl - mine;
+      for (int j = 0; j < wq; ++j) pre += red_i[j];
+      const int base = red_i[0] + red_i[1] + red_i[2] + red_i[3];
+      for (int kb = kb0; kb < kb1; ++kb)
+        if (selected(kb)) out_idx[pre++] = kb;
       if (et == 0) *out_cnt = base;
+    }
+    if (A.dbg_t && et == 0 && (blockIdx.x & 15) == 0) {
+      long long* d = A.dbg_t + (blockIdx.x >> 4) * 6;
+      d[0] = t_start; d[1] = t_first; d[2] = t_tiles; d[3] = clock64(); d[4] = ntiles; d[5] = qb;
     }
   }
 
