@@ -147,7 +147,8 @@ int check_common(int dtype, int hq, int hk, int head_dim, int block_size) {
 }
 
 // Work-item counter of the persistent attention kernel (inside the 256-byte error block).
-constexpr int64_t kCounterOffset = 64;
+constexpr int64_t kCounterOffset = 64;         // attention work-item counter
+constexpr int64_t kSearchCounterOffset = 128;  // persistent search work-item counter
 
 int sm_count(int* out) {
   int dev = 0;
@@ -250,7 +251,34 @@ int run_search(const Geometry& g, const void* q, const void* k, const int64_t qs
   }
   A.dbg_t = dbg_t;
   const unsigned grid = (unsigned)L.tiles * (unsigned)g.hq;
-  if (g.dtype == FPB_BF16) {
+  const size_t psmem = search_p_smem_bytes(L.cap);
+  const bool persistent = L.cap <= kSearchMaxCap && psmem <= 227 * 1024 && !dbg_t &&
+                          std::getenv("FLASHPREFILL_B200_SEARCH_PER_ITEM") == nullptr;
+  if (persistent) {
+    A.counter = reinterpret_cast<int*>(ws + L.err + kSearchCounterOffset);
+    A.total_items = (int)grid;
+    FPB_CUDA(cudaMemsetAsync(A.counter, 0, sizeof(int), stream));
+    int sms = 0;
+    FPB_TRY(sm_count(&sms));
+    const unsigned pgrid = (unsigned)std::min<long long>(sms, grid);
+    {
+      cudaFuncAttributes fa{};
+      FPB_CUDA(cudaFuncGetAttributes(&fa, g.dtype == FPB_BF16 ? (const void*)block_search_persistent_kernel<__nv_bfloat16>
+                                                               : (const void*)block_search_persistent_kernel<__half>));
+      if (fa.numRegs != kSearchPLaunchRegs || fa.maxThreadsPerBlock < kSearchPThreads)
+        return fail(FPB_ECUDA,
+                    "search kernel compiled with %d registers/thread (%d expected by its register split), "
+                    "at most %d threads per block (%d needed), %zu bytes static shared memory",
+                    fa.numRegs, kSearchPLaunchRegs, fa.maxThreadsPerBlock, kSearchPThreads, fa.sharedSizeBytes);
+    }
+    if (g.dtype == FPB_BF16) {
+      FPB_TRY(set_smem(block_search_persistent_kernel<__nv_bfloat16>, psmem));
+      block_search_persistent_kernel<__nv_bfloat16><<<pgrid, kSearchPThreads, psmem, stream>>>(tm_q, tm_mk, A);
+    } else {
+      FPB_TRY(set_smem(block_search_persistent_kernel<__half>, psmem));
+      block_search_persistent_kernel<__half><<<pgrid, kSearchPThreads, psmem, stream>>>(tm_q, tm_mk, A);
+    }
+  } else if (g.dtype == FPB_BF16) {
     FPB_TRY(set_smem(block_search_kernel<__nv_bfloat16>, smem));
     block_search_kernel<__nv_bfloat16><<<grid, kSearchThreads, smem, stream>>>(tm_q, tm_mk, A);
   } else {

@@ -42,6 +42,8 @@ struct SearchArgs {
   int32_t* idx;     // [hq][tiles_ub][cap]
   int32_t* cnt;     // [hq][tiles_ub]
   long long* dbg_t; // optional phase timestamps of every 16th CTA (debug)
+  int* counter;     // persistent kernel: work-item counter, zero at launch
+  int total_items;  // persistent kernel: tiles_ub * hq
 };
 
 constexpr int kSearchThreads = 192;
@@ -53,23 +55,26 @@ __host__ __device__ constexpr size_t search_smem_bytes(int cap) {
   return 3 * (size_t)kTileBytes + 8 * (size_t)cap + (size_t)((cap + 31) / 32) * 4 + 384 + 1024;
 }
 
-// Sum / max over the 128 epilogue threads (warps 2..5); uses named barrier 1.
+// Sum / max over a group of 128 threads (four warps from warp `base`), using named barrier
+// `bar` (the group's warps only).
+template <int kBase = 2, int kBar = 1>
 __device__ __forceinline__ float epi_reduce_sum(float v, float* red) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int wq = (threadIdx.x >> 5) - 2;
-  named_bar_sync(1, 128);
+  const int wq = (threadIdx.x >> 5) - kBase;
+  named_bar_sync(kBar, 128);
   if ((threadIdx.x & 31) == 0) red[wq] = v;
-  named_bar_sync(1, 128);
+  named_bar_sync(kBar, 128);
   return (red[0] + red[1]) + (red[2] + red[3]);
 }
+template <int kBase = 2, int kBar = 1>
 __device__ __forceinline__ float epi_reduce_max(float v, float* red) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  const int wq = (threadIdx.x >> 5) - 2;
-  named_bar_sync(1, 128);
+  const int wq = (threadIdx.x >> 5) - kBase;
+  named_bar_sync(kBar, 128);
   if ((threadIdx.x & 31) == 0) red[wq] = v;
-  named_bar_sync(1, 128);
+  named_bar_sync(kBar, 128);
   return fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
 }
 
@@ -366,6 +371,432 @@ __global__ void __launch_bounds__(kSearchThreads, 1)
     if (A.dbg_t && et == 0 && (blockIdx.x & 15) == 0) {
       long long* d = A.dbg_t + (blockIdx.x >> 4) * 6;
       d[0] = t_start; d[1] = t_first; d[2] = t_tiles; d[3] = clock64(); d[4] = ntiles; d[5] = qb;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+  if (threadIdx.x == 0 && *abort) raise_error(A.P.err, kErrWaitTimeout);
+}
+
+// ---------------------------------------------------------------------------------------
+// Persistent variant (sequences of up to kSearchMaxCap blocks): one CTA per SM loops over
+// the same (query block, head) items, fetched heavy-first from an atomic counter, so the
+// per-item latencies overlap instead of adding up:
+//   warp 0      scheduler + TMA producer: item ring, query block (2 slots), pooled-key tiles
+//               (2 stages)
+//   warp 1      TMEM owner + tcgen05.mma issuer (double-buffered accumulator)
+//   warps 4-7 / 8-11  tile epilogue groups 0 / 1 (the tiles with even / odd global index):
+//               per key block m and p (as above) into per-item arrays (double-buffered, so
+//               the next item's tiles proceed while ...)
+//   warps 12-15 ... the previous item is normalised, thresholded and compacted.
+// Warps 2 and 3 are idle: every SM sub-partition (warp % 4) then holds one role or idle
+// warp, two epilogue warps and one selection warp, which matters because each
+// sub-partition has its own quarter of the register file.
+constexpr int kSearchPThreads = 512;
+// Register split: compiled for 128 (= 65536 / 512); role, idle and selection warps give
+// back to 64, the epilogue warps grow to 192: per sub-partition 64 + 64 + 2*192 = 4*128.
+constexpr int kSearchPLaunchRegs = 128, kSearchPRoleRegs = 64, kSearchPEpiRegs = 192;
+static_assert(256 * kSearchPRoleRegs + 256 * kSearchPEpiRegs <= kSearchPThreads * kSearchPLaunchRegs, "split");
+constexpr int kSearchRing = 4;
+constexpr int kSearchMaxCap = 4096;
+
+__host__ __device__ constexpr size_t search_p_smem_bytes(int cap) {
+  // Q x2, pooled keys x2, two item slots of (m, p, top-k marks), barriers / ring, alignment
+  return 4 * (size_t)kTileBytes + 2 * (8 * (size_t)cap + (size_t)((cap + 31) / 32) * 4) + 1024 + 1024;
+}
+
+struct SearchItem {
+  int valid;  // 0: no more work, 1: item, 2: empty slot of the grid (skip)
+  int fast;   // every causal block selected (last-N rows or alpha <= 0): no tiles
+  int start, len, tile_base, bcoord, qb, h;
+  int pad[8];
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kSearchPThreads, 1)
+    block_search_persistent_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_mk,
+                                   const SearchArgs A) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                   // [2]
+  uint8_t* sMK = smem + 2 * kTileBytes;  // [2]
+  const int cap = A.P.cap;
+  const int ncw = (cap + 31) / 32;
+  float* arr = reinterpret_cast<float*>(smem + 4 * kTileBytes);      // [2]{m[cap], p[cap]}
+  uint32_t* marks_all = reinterpret_cast<uint32_t*>(arr + 4 * cap);  // [2][ncw]
+  uint8_t* misc = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(marks_all + 2 * ncw) + 15) & ~uintptr_t(15));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(misc);
+  uint64_t* item_full = bars + 0;    // [ring]
+  uint64_t* item_empty = bars + 4;   // [ring]
+  uint64_t* q_full = bars + 8;       // [2]
+  uint64_t* q_empty = bars + 10;     // [2]
+  uint64_t* mk_full = bars + 12;     // [2]
+  uint64_t* mk_empty = bars + 14;    // [2]
+  uint64_t* acc_full = bars + 16;    // [2]
+  uint64_t* acc_empty = bars + 18;   // [2]
+  uint64_t* arr_full = bars + 20;    // [2] an item's m / p complete
+  uint64_t* arr_empty = bars + 22;   // [2] an item's m / p consumed
+  uint64_t* mma_done = bars + 24;
+  SearchItem* ring = reinterpret_cast<SearchItem*>(misc + 256);  // [ring]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 512);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* mrun = reinterpret_cast<int*>(tmem_slot + 2);     // [2] running max per item slot (ordered int)
+  float* red = reinterpret_cast<float*>(tmem_slot + 4);  // [4] selection-group reductions
+  int* red_i = reinterpret_cast<int*>(tmem_slot + 8);    // [4]
+  int* red_k = reinterpret_cast<int*>(tmem_slot + 12);   // [4]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kSearchRing; ++i) {
+      mbar_init(item_full + i, 1);
+      mbar_init(item_empty + i, 1 + 256 + 128);  // MMA issuer, tile epilogue, selection
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(q_full + i, 1);
+      mbar_init(q_empty + i, 1);
+      mbar_init(mk_full + i, 1);
+      mbar_init(mk_empty + i, 1);
+      mbar_init(acc_full + i, 1);
+      mbar_init(acc_empty + i, 128);
+      mbar_init(arr_full + i, 256);
+      mbar_init(arr_empty + i, 128);
+      mrun[i] = float_to_ordered(-INFINITY);
+    }
+    mbar_init(mma_done, 1);
+    *abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int group = A.P.hq / A.P.hk;
+
+  const bool epi_warp = warp >= 4 && warp < 12;
+  if (warp == 0) {
+    // ------------------------------------------------------------ scheduler + TMA producer
+    regs_dec<kSearchPRoleRegs>();
+    if (lane == 0) {
+      prefetch_tmap(&tm_q);
+      prefetch_tmap(&tm_mk);
+      uint32_t it = 0, qn = 0, tn = 0;
+      bool ok = true;
+      while (ok) {
+        const int slot = it % kSearchRing;
+        if (!mbar_wait_sleep(item_empty + slot, ((it / kSearchRing) & 1) ^ 1, abort)) break;
+        SearchItem f{};
+        const int id = atomicAdd(A.counter, 1);
+        if (id >= A.total_items) {
+          f.valid = 0;
+        } else {
+          SeqInfo sq;
+          int qb;
+          const int tile = id / A.P.hq;
+          if (!decode_item(A.P, tile, sq, qb)) {
+            f.valid = 2;
+          } else {
+            f.valid = 1;
+            f.fast = (qb >= sq.nb - A.last_n || !(A.alpha > 0.f)) ? 1 : 0;
+            f.start = sq.start;
+            f.len = sq.len;
+            f.tile_base = sq.tile_base;
+            f.bcoord = sq.bcoord;
+            f.qb = qb;
+            f.h = id - tile * A.P.hq;
+          }
+        }
+        ring[slot] = f;
+        mbar_arrive(item_full + slot);
+        ++it;
+        if (f.valid == 0) break;
+        if (f.valid != 1 || f.fast) continue;
+        const int qs = qn & 1;
+        if (!mbar_wait_sleep(q_empty + qs, ((qn >> 1) & 1) ^ 1, abort)) break;
+        ++qn;
+        const int qrow = f.start + f.qb * kBlock;
+        mbar_arrive_expect_tx(q_full + qs, kTileBytes);
+        tma_load_4d(sQ + qs * kTileBytes, &tm_q, q_full + qs, 0, f.h, qrow, f.bcoord);
+        tma_load_4d(sQ + qs * kTileBytes + kHalfTile, &tm_q, q_full + qs, 64, f.h, qrow, f.bcoord);
+        const int hk = f.h / group, ntiles = f.qb / kBlock + 1;
+        for (int t = 0; t < ntiles; ++t, ++tn) {
+          const int st = tn & 1;
+          if (!mbar_wait_sleep(mk_empty + st, ((tn >> 1) & 1) ^ 1, abort)) { ok = false; break; }
+          mbar_arrive_expect_tx(mk_full + st, kTileBytes);
+          uint8_t* dst = sMK + st * kTileBytes;
+          const int mrow = f.tile_base + t * kBlock;
+          tma_load_4d(dst, &tm_mk, mk_full + st, 0, hk, mrow, 0);
+          tma_load_4d(dst + kHalfTile, &tm_mk, mk_full + st, 64, hk, mrow, 0);
+        }
+      }
+      if (*abort) {  // let loads still in flight land before the CTA exits
+        volatile int no_abort = 0;
+        for (int sl = 0; sl < 2; ++sl) {
+          const uint32_t nt = (tn + 1 - sl) >> 1, nq = (qn + 1 - sl) >> 1;
+          if (nt) mbar_wait(mk_full + sl, (nt - 1) & 1, &no_abort);
+          if (nq) mbar_wait(q_full + sl, (nq - 1) & 1, &no_abort);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    regs_dec<kSearchPRoleRegs>();
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(128, 128, DT<T>::is_bf16, false);
+      uint32_t it = 0, qc = 0, tc = 0;
+      bool ok = true;
+      while (ok) {
+        const int slot = it % kSearchRing;
+        if (!mbar_wait_sleep(item_full + slot, (it / kSearchRing) & 1, abort)) break;
+        const SearchItem f = ring[slot];
+        if (f.valid == 0) break;
+        if (f.valid == 1 && !f.fast) {
+          const int qs = qc & 1;
+          if (!mbar_wait(q_full + qs, (qc >> 1) & 1, abort)) break;
+          const uint32_t q_base = smem_u32(sQ + qs * kTileBytes);
+          const int ntiles = f.qb / kBlock + 1;
+          for (int t = 0; t < ntiles; ++t, ++tc) {
+            const int st = tc & 1;
+            if (!mbar_wait(mk_full + st, (tc >> 1) & 1, abort)) { ok = false; break; }
+            if (!mbar_wait(acc_empty + st, ((tc >> 1) & 1) ^ 1, abort)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t a_base = smem_u32(sMK + st * kTileBytes);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+              const uint32_t off = (ks >> 2) * kHalfTile + (ks & 3) * 32;
+              umma_ss(tmem + st * 128, sdesc_sw128(a_base + off, 16, 1024), sdesc_sw128(q_base + off, 16, 1024),
+                      idesc, ks > 0);
+            }
+            umma_commit(mk_empty + st);
+            umma_commit(acc_full + st);
+          }
+          if (!ok) break;
+          umma_commit(q_empty + qs);
+          ++qc;
+        }
+        mbar_arrive(item_empty + slot);
+        ++it;
+      }
+      umma_commit(mma_done);
+      volatile int no_abort = 0;
+      mbar_wait(mma_done, 0, &no_abort);
+    }
+  } else if (warp < 4) {
+    regs_dec<kSearchPRoleRegs>();  // idle
+  } else if (epi_warp) {
+    // ------------------------------------------------------------ tile epilogue (warps 4..11)
+    regs_inc<kSearchPEpiRegs>();
+    const int eg = (warp - 4) >> 2;     // group: tiles with tc % 2 == eg
+    const int quad = warp & 3;
+    const int lrow = quad * 32 + lane;  // TMEM lane = key block within the tile
+    const float c = A.c;
+    uint32_t it = 0, tc = 0, an = 0;
+    while (true) {
+      const int slot = it % kSearchRing;
+      if (!mbar_wait_warp_sleep(item_full + slot, (it / kSearchRing) & 1, abort)) break;
+      const SearchItem f = ring[slot];
+      if (f.valid == 0) break;
+      bool ok = true;
+      if (f.valid == 1 && !f.fast) {
+        const int a = an & 1;
+        if (!mbar_wait_warp_sleep(arr_empty + a, ((an >> 1) & 1) ^ 1, abort)) break;
+        ++an;
+        float* m_arr = arr + a * 2 * cap;
+        float* p_arr = m_arr + cap;
+        int* mr = mrun + a;
+        const int qb = f.qb;
+        const int vr = min(kBlock, f.len - qb * kBlock);  // valid query rows of this block
+        const int ntiles = qb / kBlock + 1;
+        for (int t = 0; t < ntiles; ++t, ++tc) {
+          const int acc = tc & 1;
+          if (acc != eg) continue;  // the other group's tile
+          if (!mbar_wait_warp_sleep(acc_full + acc, (tc >> 1) & 1, abort)) { ok = false; break; }
+          tc_fence_after();
+          const int kb = t * kBlock + lrow;
+          const uint32_t taddr = tmem + acc * 128 + ((uint32_t)(quad * 32) << 16);
+          uint32_t ua[32], ub[32], uc[32], ud[32];
+          tmem_ld32(taddr, ua);
+          tmem_ld32(taddr + 32, ub);
+          tmem_ld32(taddr + 64, uc);
+          tmem_ld32(taddr + 96, ud);
+          tmem_ld_wait();
+          tc_fence_before();
+          mbar_arrive(acc_empty + acc);  // the accumulator may be overwritten by tile tc + 2
+#define FPB_S(i) __uint_as_float((i) < 32 ? ua[(i)] : (i) < 64 ? ub[(i) - 32] : (i) < 96 ? uc[(i) - 64] : ud[(i) - 96])
+          float mx, s127;
+          if (vr == kBlock) {
+            float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 128; i += 4) {
+              m0 = max3(m0, FPB_S(i), FPB_S(i + 1));
+              m1 = max3(m1, FPB_S(i + 2), FPB_S(i + 3));
+            }
+            mx = fmaxf(m0, m1);
+            s127 = FPB_S(127);
+          } else {  // a sequence's last, partial query block: padded rows have q = 0, s = 0
+            mx = 0.f;
+#pragma unroll
+            for (int i = 0; i < 128; ++i)
+              if (i < vr) mx = fmaxf(mx, FPB_S(i));
+            s127 = 0.f;
+          }
+          const bool causal = kb <= qb;
+          const bool diag = kb == qb;
+          float m = -INFINITY;
+          if (causal) m = __fmul_rn(diag ? s127 : mx, c);
+          float wm = m;  // running lower bound of the row maximum
+#pragma unroll
+          for (int o = 16; o; o >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, o));
+          const float m_est = fmaxf(wm, ordered_to_float(*(volatile int*)mr));
+          if (lane == 0 && wm > -INFINITY) atomicMax(mr, float_to_ordered(wm));
+          const bool cand = causal && (m >= m_est + A.cand_off);
+          float p = 0.f;
+          if (__any_sync(0xffffffffu, cand && !diag)) {
+            const float nm = -m;
+            float p0 = 0.f, p1 = 0.f;
+            if (vr == kBlock) {
+              // one pair in four on the FMA pipe (exp2_poly2, relative error ~1e-4), the rest
+              // by ex2.approx: the sum only has to resolve the 1e-3 threshold band
+#pragma unroll
+              for (int i = 0; i < 128; i += 2) {
+                float x0, x1, e0, e1;
+                fma2(x0, x1, FPB_S(i), FPB_S(i + 1), c, c, nm, nm);
+                if (((i >> 1) & 3) == 3) {
+                  exp2_poly2(x0, x1, e0, e1);
+                } else {
+                  e0 = ex2_approx(x0);
+                  e1 = ex2_approx(x1);
+                }
+                add2(p0, p1, p0, p1, e0, e1);
+              }
+              p = p0 + p1;
+            } else {
+#pragma unroll
+              for (int i = 0; i < 128; ++i)
+                if (i < vr) p += ex2_approx(__fmaf_rn(FPB_S(i), c, nm));
+              p += (float)(kBlock - vr) * ex2_approx(-m);
+            }
+          }
+#undef FPB_S
+          if (diag) p = 1.f;
+          if (causal) {
+            m_arr[kb] = m;
+            p_arr[kb] = cand ? p : -1.f;
+          }
+        }
+        if (!ok) break;
+        mbar_arrive(arr_full + a);
+      }
+      mbar_arrive(item_empty + slot);
+      ++it;
+    }
+  } else {
+    // ------------------------------------------------------------ selection (warps 12..15)
+    regs_dec<kSearchPRoleRegs>();
+    const int es = threadIdx.x - 384;  // 0..127
+    const int wq = warp - 12;
+    uint32_t it = 0, an = 0;
+    while (true) {
+      const int slot = it % kSearchRing;
+      if (!mbar_wait_warp_sleep(item_full + slot, (it / kSearchRing) & 1, abort)) break;
+      const SearchItem f = ring[slot];
+      if (f.valid == 0) break;
+      if (f.valid == 1) {
+        const int qb = f.qb;
+        const int row = f.tile_base + qb;
+        int32_t* out_idx = A.idx + ((int64_t)f.h * A.P.tiles_ub + row) * cap;
+        int32_t* out_cnt = A.cnt + (int64_t)f.h * A.P.tiles_ub + row;
+        if (f.fast) {  // every causal block
+          for (int kb = es; kb <= qb; kb += 128) out_idx[kb] = kb;
+          if (es == 0) *out_cnt = qb + 1;
+        } else {
+          const int a = an & 1;
+          if (!mbar_wait_warp_sleep(arr_full + a, (an >> 1) & 1, abort)) break;
+          ++an;
+          float* m_arr = arr + a * 2 * cap;
+          float* p_arr = m_arr + cap;
+          uint32_t* marks = marks_all + a * ncw;
+          const float M = ordered_to_float(*(volatile int*)(mrun + a));
+          // pw >= alpha * max pw  (see the per-item kernel above)
+          float best = 0.f;
+          for (int kb = es; kb <= qb; kb += 128) {
+            const float pv = p_arr[kb];
+            const float pw = pv >= 0.f ? __fmul_rn(pv, ex2_approx(__fsub_rn(m_arr[kb], M))) : -1.f;
+            p_arr[kb] = pw;
+            best = fmaxf(best, pw);
+          }
+          const float thr = __fmul_rn(epi_reduce_max<12, 2>(best, red), A.alpha);
+          const int nwords = (qb + 1 + 31) / 32;
+          const int kbudget = min(A.min_budget, qb + 1);
+          if (kbudget > 0) {
+            for (int wd = es; wd < nwords; wd += 128) marks[wd] = 0u;
+            named_bar_sync(2, 128);
+          }
+          for (int r2 = 0; r2 < kbudget; ++r2) {
+            float bv = -INFINITY;
+            int bk = 0x7fffffff;
+            for (int kb = es; kb <= qb; kb += 128) {
+              if (marks[kb >> 5] & (1u << (kb & 31))) continue;
+              const float v = fmaxf(p_arr[kb], 0.f);
+              if (v > bv || (v == bv && kb < bk)) { bv = v; bk = kb; }
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+              const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+              const int ok2 = __shfl_xor_sync(0xffffffffu, bk, o);
+              if (ov > bv || (ov == bv && ok2 < bk)) { bv = ov; bk = ok2; }
+            }
+            if (lane == 0) { red[wq] = bv; red_k[wq] = bk; }
+            named_bar_sync(2, 128);
+            if (es == 0) {
+              float v0 = red[0];
+              int k0 = red_k[0];
+              for (int j = 1; j < 4; ++j)
+                if (red[j] > v0 || (red[j] == v0 && red_k[j] < k0)) { v0 = red[j]; k0 = red_k[j]; }
+              if (k0 <= qb) marks[k0 >> 5] |= 1u << (k0 & 31);
+            }
+            named_bar_sync(2, 128);
+          }
+          const int chunk = (qb + 128) / 128;
+          const int kb0 = es * chunk, kb1 = min(qb + 1, kb0 + chunk);
+          auto selected = [&](int kb) -> bool {
+            const float pw = p_arr[kb];
+            bool sel = (pw >= 0.f && pw >= thr) || kb < A.sink || (qb - kb) < A.window;
+            if (kbudget > 0) sel = sel || ((marks[kb >> 5] >> (kb & 31)) & 1u);
+            return sel;
+          };
+          int mine = 0;
+          for (int kb = kb0; kb < kb1; ++kb) mine += selected(kb);
+          int incl = mine;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+          }
+          if (lane == 31) red_i[wq] = incl;
+          named_bar_sync(2, 128);
+          int pre = incl - mine;
+          for (int j = 0; j < wq; ++j) pre += red_i[j];
+          const int total = red_i[0] + red_i[1] + red_i[2] + red_i[3];
+          for (int kb = kb0; kb < kb1; ++kb)
+            if (selected(kb)) out_idx[pre++] = kb;
+          if (es == 0) *out_cnt = total;
+          named_bar_sync(2, 128);  // every thread has read M, red_i and this item's arrays
+          if (es == 0) mrun[a] = float_to_ordered(-INFINITY);
+          mbar_arrive(arr_empty + a);
+        }
+      }
+      mbar_arrive(item_empty + slot);
+      ++it;
     }
   }
 
