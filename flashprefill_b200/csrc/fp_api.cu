@@ -271,12 +271,26 @@ int run_search(const Geometry& g, const void* q, const void* k, const int64_t qs
                     "at most %d threads per block (%d needed), %zu bytes static shared memory",
                     fa.numRegs, kSearchPLaunchRegs, fa.maxThreadsPerBlock, kSearchPThreads, fa.sharedSizeBytes);
     }
+    unsigned long long* sprof = nullptr;
+    if (std::getenv("FLASHPREFILL_B200_SEARCH_PROFILE")) {
+      FPB_CUDA(cudaMalloc(&sprof, sizeof(unsigned long long) * kSpSlots));
+      FPB_CUDA(cudaMemsetAsync(sprof, 0, sizeof(unsigned long long) * kSpSlots, stream));
+    }
+    A.prof = sprof;
     if (g.dtype == FPB_BF16) {
       FPB_TRY(set_smem(block_search_persistent_kernel<__nv_bfloat16>, psmem));
       block_search_persistent_kernel<__nv_bfloat16><<<pgrid, kSearchPThreads, psmem, stream>>>(tm_q, tm_mk, A);
     } else {
       FPB_TRY(set_smem(block_search_persistent_kernel<__half>, psmem));
       block_search_persistent_kernel<__half><<<pgrid, kSearchPThreads, psmem, stream>>>(tm_q, tm_mk, A);
+    }
+    if (sprof) {
+      unsigned long long h[kSpSlots];
+      FPB_CUDA(cudaMemcpyAsync(h, sprof, sizeof(h), cudaMemcpyDeviceToHost, stream));
+      FPB_CUDA(cudaStreamSynchronize(stream));
+      fprintf(stderr, "[fpb search profile] grid=%u\n", pgrid);
+      for (int i = 0; i < kSpSlots; ++i) fprintf(stderr, "[fpb search profile] %-22s %llu\n", kSearchProfNames[i], h[i]);
+      cudaFree(sprof);
     }
   } else if (g.dtype == FPB_BF16) {
     FPB_TRY(set_smem(block_search_kernel<__nv_bfloat16>, smem));

@@ -44,7 +44,21 @@ struct SearchArgs {
   long long* dbg_t; // optional phase timestamps of every 16th CTA (debug)
   int* counter;     // persistent kernel: work-item counter, zero at launch
   int total_items;  // persistent kernel: tiles_ub * hq
+  unsigned long long* prof;  // persistent kernel: optional per-phase cycle sums (kSpSlots)
 };
+// Instrumentation of the persistent search: compiled in with -DFPB_SEARCH_PROFILE=1, enabled
+// at run time with FLASHPREFILL_B200_SEARCH_PROFILE=1.
+#ifndef FPB_SEARCH_PROFILE
+#define FPB_SEARCH_PROFILE 0
+#endif
+enum SearchProf {
+  kSpProdItem, kSpProdQ, kSpProdMk, kSpMmaQ, kSpMmaMk, kSpMmaAcc, kSpEpiItem, kSpEpiArr, kSpEpiAcc, kSpEpiLd,
+  kSpEpiMax, kSpEpiExp, kSpEpiTiles, kSpEpiExpTiles, kSpSelItem, kSpSelArr, kSpSelWork, kSpCta, kSpSlots
+};
+static const char* const kSearchProfNames[kSpSlots] = {
+    "prod_wait_item_slot", "prod_wait_q_slot", "prod_wait_mk_stage", "mma_wait_q", "mma_wait_mk", "mma_wait_acc",
+    "epi_wait_item", "epi_wait_arrays", "epi_wait_acc", "epi_tmem_ld", "epi_max_pass", "epi_exp_pass", "epi_tiles",
+    "epi_tiles_with_exp", "sel_wait_item", "sel_wait_arrays", "sel_work", "cta_cycles"};
 
 constexpr int kSearchThreads = 192;
 constexpr uint32_t kTileBytes = 128 * 128 * 2;  // one 128x128 16-bit tile (two 64-column TMA boxes)
@@ -421,6 +435,25 @@ template <typename T>
 __global__ void __launch_bounds__(kSearchPThreads, 1)
     block_search_persistent_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_mk,
                                    const SearchArgs A) {
+#if FPB_SEARCH_PROFILE
+  const long long t_k0 = clock64();
+  // per-role accumulators (one recording thread per role), flushed at the end
+  unsigned long long pacc[kSpSlots] = {};
+#define SP_TW(slot, call)                        \
+  ({                                             \
+    const long long t0_ = clock64();             \
+    const bool r_ = (call);                      \
+    if (A.prof) pacc[slot] += clock64() - t0_;   \
+    r_;                                          \
+  })
+#define SP_T() clock64()
+#define SP_ON (A.prof != nullptr)
+#else
+#define SP_TW(slot, call) (call)
+#define SP_T() 0ll
+#define SP_ON false
+  unsigned long long pacc[kSpSlots];
+#endif
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                   // [2]
@@ -493,7 +526,7 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
       bool ok = true;
       while (ok) {
         const int slot = it % kSearchRing;
-        if (!mbar_wait_sleep(item_empty + slot, ((it / kSearchRing) & 1) ^ 1, abort)) break;
+        if (!SP_TW(kSpProdItem, mbar_wait_sleep(item_empty + slot, ((it / kSearchRing) & 1) ^ 1, abort))) break;
         SearchItem f{};
         const int id = atomicAdd(A.counter, 1);
         if (id >= A.total_items) {
@@ -521,7 +554,7 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
         if (f.valid == 0) break;
         if (f.valid != 1 || f.fast) continue;
         const int qs = qn & 1;
-        if (!mbar_wait_sleep(q_empty + qs, ((qn >> 1) & 1) ^ 1, abort)) break;
+        if (!SP_TW(kSpProdQ, mbar_wait_sleep(q_empty + qs, ((qn >> 1) & 1) ^ 1, abort))) break;
         ++qn;
         const int qrow = f.start + f.qb * kBlock;
         mbar_arrive_expect_tx(q_full + qs, kTileBytes);
@@ -530,7 +563,7 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
         const int hk = f.h / group, ntiles = f.qb / kBlock + 1;
         for (int t = 0; t < ntiles; ++t, ++tn) {
           const int st = tn & 1;
-          if (!mbar_wait_sleep(mk_empty + st, ((tn >> 1) & 1) ^ 1, abort)) { ok = false; break; }
+          if (!SP_TW(kSpProdMk, mbar_wait_sleep(mk_empty + st, ((tn >> 1) & 1) ^ 1, abort))) { ok = false; break; }
           mbar_arrive_expect_tx(mk_full + st, kTileBytes);
           uint8_t* dst = sMK + st * kTileBytes;
           const int mrow = f.tile_base + t * kBlock;
@@ -561,13 +594,13 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
         if (f.valid == 0) break;
         if (f.valid == 1 && !f.fast) {
           const int qs = qc & 1;
-          if (!mbar_wait(q_full + qs, (qc >> 1) & 1, abort)) break;
+          if (!SP_TW(kSpMmaQ, mbar_wait(q_full + qs, (qc >> 1) & 1, abort))) break;
           const uint32_t q_base = smem_u32(sQ + qs * kTileBytes);
           const int ntiles = f.qb / kBlock + 1;
           for (int t = 0; t < ntiles; ++t, ++tc) {
             const int st = tc & 1;
-            if (!mbar_wait(mk_full + st, (tc >> 1) & 1, abort)) { ok = false; break; }
-            if (!mbar_wait(acc_empty + st, ((tc >> 1) & 1) ^ 1, abort)) { ok = false; break; }
+            if (!SP_TW(kSpMmaMk, mbar_wait(mk_full + st, (tc >> 1) & 1, abort))) { ok = false; break; }
+            if (!SP_TW(kSpMmaAcc, mbar_wait(acc_empty + st, ((tc >> 1) & 1) ^ 1, abort))) { ok = false; break; }
             tc_fence_after();
             const uint32_t a_base = smem_u32(sMK + st * kTileBytes);
 #pragma unroll
@@ -602,13 +635,13 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
     uint32_t it = 0, tc = 0, an = 0;
     while (true) {
       const int slot = it % kSearchRing;
-      if (!mbar_wait_warp_sleep(item_full + slot, (it / kSearchRing) & 1, abort)) break;
+      if (!SP_TW(kSpEpiItem, mbar_wait_warp_sleep(item_full + slot, (it / kSearchRing) & 1, abort))) break;
       const SearchItem f = ring[slot];
       if (f.valid == 0) break;
       bool ok = true;
       if (f.valid == 1 && !f.fast) {
         const int a = an & 1;
-        if (!mbar_wait_warp_sleep(arr_empty + a, ((an >> 1) & 1) ^ 1, abort)) break;
+        if (!SP_TW(kSpEpiArr, mbar_wait_warp_sleep(arr_empty + a, ((an >> 1) & 1) ^ 1, abort))) break;
         ++an;
         float* m_arr = arr + a * 2 * cap;
         float* p_arr = m_arr + cap;
@@ -619,8 +652,9 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
         for (int t = 0; t < ntiles; ++t, ++tc) {
           const int acc = tc & 1;
           if (acc != eg) continue;  // the other group's tile
-          if (!mbar_wait_warp_sleep(acc_full + acc, (tc >> 1) & 1, abort)) { ok = false; break; }
+          if (!SP_TW(kSpEpiAcc, mbar_wait_warp_sleep(acc_full + acc, (tc >> 1) & 1, abort))) { ok = false; break; }
           tc_fence_after();
+          const long long te1 = SP_T();
           const int kb = t * kBlock + lrow;
           const uint32_t taddr = tmem + acc * 128 + ((uint32_t)(quad * 32) << 16);
           uint32_t ua[32], ub[32], uc[32], ud[32];
@@ -631,6 +665,7 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
           tmem_ld_wait();
           tc_fence_before();
           mbar_arrive(acc_empty + acc);  // the accumulator may be overwritten by tile tc + 2
+          const long long te2 = SP_T();
 #define FPB_S(i) __uint_as_float((i) < 32 ? ua[(i)] : (i) < 64 ? ub[(i) - 32] : (i) < 96 ? uc[(i) - 64] : ud[(i) - 96])
           float mx, s127;
           if (vr == kBlock) {
@@ -660,7 +695,9 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
           if (lane == 0 && wm > -INFINITY) atomicMax(mr, float_to_ordered(wm));
           const bool cand = causal && (m >= m_est + A.cand_off);
           float p = 0.f;
-          if (__any_sync(0xffffffffu, cand && !diag)) {
+          const long long te3 = SP_T();
+          const bool any_exp = __any_sync(0xffffffffu, cand && !diag);
+          if (any_exp) {
             const float nm = -m;
             float p0 = 0.f, p1 = 0.f;
             if (vr == kBlock) {
@@ -692,6 +729,14 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
             m_arr[kb] = m;
             p_arr[kb] = cand ? p : -1.f;
           }
+          if (SP_ON) {
+            const long long te4 = SP_T();
+            pacc[kSpEpiLd] += te2 - te1;
+            pacc[kSpEpiMax] += te3 - te2;
+            pacc[kSpEpiExp] += te4 - te3;
+            pacc[kSpEpiTiles] += 1;
+            pacc[kSpEpiExpTiles] += any_exp;
+          }
         }
         if (!ok) break;
         mbar_arrive(arr_full + a);
@@ -707,7 +752,8 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
     uint32_t it = 0, an = 0;
     while (true) {
       const int slot = it % kSearchRing;
-      if (!mbar_wait_warp_sleep(item_full + slot, (it / kSearchRing) & 1, abort)) break;
+      if (!SP_TW(kSpSelItem, mbar_wait_warp_sleep(item_full + slot, (it / kSearchRing) & 1, abort))) break;
+      const long long ts0 = SP_T();
       const SearchItem f = ring[slot];
       if (f.valid == 0) break;
       if (f.valid == 1) {
@@ -720,7 +766,7 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
           if (es == 0) *out_cnt = qb + 1;
         } else {
           const int a = an & 1;
-          if (!mbar_wait_warp_sleep(arr_full + a, (an >> 1) & 1, abort)) break;
+          if (!SP_TW(kSpSelArr, mbar_wait_warp_sleep(arr_full + a, (an >> 1) & 1, abort))) break;
           ++an;
           float* m_arr = arr + a * 2 * cap;
           float* p_arr = m_arr + cap;
@@ -728,6 +774,7 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
           const float M = ordered_to_float(*(volatile int*)(mrun + a));
           // pw >= alpha * max pw  (see the per-item kernel above)
           float best = 0.f;
+#pragma unroll 4
           for (int kb = es; kb <= qb; kb += 128) {
             const float pv = p_arr[kb];
             const float pw = pv >= 0.f ? __fmul_rn(pv, ex2_approx(__fsub_rn(m_arr[kb], M))) : -1.f;
@@ -766,39 +813,53 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
             }
             named_bar_sync(2, 128);
           }
-          const int chunk = (qb + 128) / 128;
-          const int kb0 = es * chunk, kb1 = min(qb + 1, kb0 + chunk);
+          // selection + ascending compaction: warp wq owns the contiguous key blocks
+          // [wq * span, wq * span + span), visited 32 at a time (one per lane, ballot +
+          // popcount); one barrier combines the four warp totals
+          const int span = ((qb + 1 + 127) / 128) * 32;
+          const int w0 = wq * span, w1 = min(qb + 1, w0 + span);
           auto selected = [&](int kb) -> bool {
+            if (kb >= w1) return false;
             const float pw = p_arr[kb];
             bool sel = (pw >= 0.f && pw >= thr) || kb < A.sink || (qb - kb) < A.window;
             if (kbudget > 0) sel = sel || ((marks[kb >> 5] >> (kb & 31)) & 1u);
             return sel;
           };
-          int mine = 0;
-          for (int kb = kb0; kb < kb1; ++kb) mine += selected(kb);
-          int incl = mine;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += y;
-          }
-          if (lane == 31) red_i[wq] = incl;
+          int wcount = 0;
+          for (int k0 = w0; k0 < w1; k0 += 32) wcount += __popc(__ballot_sync(0xffffffffu, selected(k0 + lane)));
+          if (lane == 0) red_i[wq] = wcount;
           named_bar_sync(2, 128);
-          int pre = incl - mine;
+          int pre = 0;
           for (int j = 0; j < wq; ++j) pre += red_i[j];
           const int total = red_i[0] + red_i[1] + red_i[2] + red_i[3];
-          for (int kb = kb0; kb < kb1; ++kb)
-            if (selected(kb)) out_idx[pre++] = kb;
+          for (int k0 = w0; k0 < w1; k0 += 32) {
+            const bool sel = selected(k0 + lane);
+            const uint32_t bal = __ballot_sync(0xffffffffu, sel);
+            if (sel) out_idx[pre + __popc(bal & ((1u << lane) - 1u))] = k0 + lane;
+            pre += __popc(bal);
+          }
           if (es == 0) *out_cnt = total;
           named_bar_sync(2, 128);  // every thread has read M, red_i and this item's arrays
           if (es == 0) mrun[a] = float_to_ordered(-INFINITY);
           mbar_arrive(arr_empty + a);
         }
       }
+      if (SP_ON) pacc[kSpSelWork] += SP_T() - ts0;
       mbar_arrive(item_empty + slot);
       ++it;
     }
   }
+  // recording threads: producer, issuer, the first epilogue thread of group 0, the first selection thread
+#if FPB_SEARCH_PROFILE
+  if (A.prof && (threadIdx.x == 0 || threadIdx.x == 32 || threadIdx.x == 128 || threadIdx.x == 384)) {
+    pacc[kSpCta] = threadIdx.x == 0 ? clock64() - t_k0 : 0;
+    for (int i = 0; i < kSpSlots; ++i)
+      if (pacc[i]) atomicAdd(A.prof + i, pacc[i]);
+  }
+#endif
+#undef SP_TW
+#undef SP_T
+#undef SP_ON
 
   tc_fence_before();
   __syncthreads();
