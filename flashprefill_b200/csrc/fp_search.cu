@@ -407,15 +407,17 @@ __global__ void __launch_bounds__(kSearchThreads, 1)
 //   warps 4-7 / 8-11  tile epilogue groups 0 / 1 (the tiles with even / odd global index):
 //               per key block m and p (as above) into per-item arrays (double-buffered, so
 //               the next item's tiles proceed while ...)
-//   warps 12-15 ... the previous item is normalised, thresholded and compacted.
+//   warps 12-15 / 16-19  selection groups 0 / 1: ... the previous items (array slot 0 / 1)
+//               are normalised, thresholded and compacted.
 // Warps 2 and 3 are idle: every SM sub-partition (warp % 4) then holds one role or idle
-// warp, two epilogue warps and one selection warp, which matters because each
+// warp, two epilogue warps and two selection warps, which matters because each
 // sub-partition has its own quarter of the register file.
-constexpr int kSearchPThreads = 512;
-// Register split: compiled for 128 (= 65536 / 512); role, idle and selection warps give
-// back to 64, the epilogue warps grow to 192: per sub-partition 64 + 64 + 2*192 = 4*128.
-constexpr int kSearchPLaunchRegs = 128, kSearchPRoleRegs = 64, kSearchPEpiRegs = 192;
-static_assert(256 * kSearchPRoleRegs + 256 * kSearchPEpiRegs <= kSearchPThreads * kSearchPLaunchRegs, "split");
+constexpr int kSearchPThreads = 640;
+// Register split: compiled for 96 (= 65536 / 640, rounded down to a multiple of 8); role,
+// idle and selection warps give back to 64, the epilogue warps grow to 144: per
+// sub-partition 3*64 + 2*144 = 480 = 5*96.
+constexpr int kSearchPLaunchRegs = 96, kSearchPRoleRegs = 64, kSearchPEpiRegs = 144;
+static_assert(384 * kSearchPRoleRegs + 256 * kSearchPEpiRegs <= kSearchPThreads * kSearchPLaunchRegs, "split");
 constexpr int kSearchRing = 4;
 constexpr int kSearchMaxCap = 4096;
 
@@ -423,6 +425,11 @@ __host__ __device__ constexpr size_t search_p_smem_bytes(int cap) {
   // Q x2, pooled keys x2, two item slots of (m, p, top-k marks), barriers / ring, alignment
   return 4 * (size_t)kTileBytes + 2 * (8 * (size_t)cap + (size_t)((cap + 31) / 32) * 4) + 1024 + 1024;
 }
+
+// Tiles of a row are visited last first (diagonal and window blocks), then from the first
+// (sink blocks): the blocks that usually hold the row maximum come first, so the running
+// estimate that lets the exp2 pass skip most key blocks is close to final early.
+__device__ __forceinline__ int tile_order(int j, int ntiles) { return j == 0 ? ntiles - 1 : j - 1; }
 
 struct SearchItem {
   int valid;  // 0: no more work, 1: item, 2: empty slot of the grid (skip)
@@ -480,15 +487,15 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 512);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* mrun = reinterpret_cast<int*>(tmem_slot + 2);     // [2] running max per item slot (ordered int)
-  float* red = reinterpret_cast<float*>(tmem_slot + 4);  // [4] selection-group reductions
-  int* red_i = reinterpret_cast<int*>(tmem_slot + 8);    // [4]
-  int* red_k = reinterpret_cast<int*>(tmem_slot + 12);   // [4]
+  float* red_all = reinterpret_cast<float*>(tmem_slot + 4);  // [2 groups][4] selection reductions
+  int* red_i_all = reinterpret_cast<int*>(tmem_slot + 12);   // [2][4]
+  int* red_k_all = reinterpret_cast<int*>(tmem_slot + 20);   // [2][4]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kSearchRing; ++i) {
       mbar_init(item_full + i, 1);
-      mbar_init(item_empty + i, 1 + 256 + 128);  // MMA issuer, tile epilogue, selection
+      mbar_init(item_empty + i, 1 + 256 + 256);  // MMA issuer, tile epilogue, selection
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(q_full + i, 1);
@@ -561,7 +568,8 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
         tma_load_4d(sQ + qs * kTileBytes, &tm_q, q_full + qs, 0, f.h, qrow, f.bcoord);
         tma_load_4d(sQ + qs * kTileBytes + kHalfTile, &tm_q, q_full + qs, 64, f.h, qrow, f.bcoord);
         const int hk = f.h / group, ntiles = f.qb / kBlock + 1;
-        for (int t = 0; t < ntiles; ++t, ++tn) {
+        for (int j = 0; j < ntiles; ++j, ++tn) {
+          const int t = tile_order(j, ntiles);
           const int st = tn & 1;
           if (!SP_TW(kSpProdMk, mbar_wait_sleep(mk_empty + st, ((tn >> 1) & 1) ^ 1, abort))) { ok = false; break; }
           mbar_arrive_expect_tx(mk_full + st, kTileBytes);
@@ -649,7 +657,8 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
         const int qb = f.qb;
         const int vr = min(kBlock, f.len - qb * kBlock);  // valid query rows of this block
         const int ntiles = qb / kBlock + 1;
-        for (int t = 0; t < ntiles; ++t, ++tc) {
+        for (int j = 0; j < ntiles; ++j, ++tc) {
+          const int t = tile_order(j, ntiles);
           const int acc = tc & 1;
           if (acc != eg) continue;  // the other group's tile
           if (!SP_TW(kSpEpiAcc, mbar_wait_warp_sleep(acc_full + acc, (tc >> 1) & 1, abort))) { ok = false; break; }
@@ -657,33 +666,33 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
           const long long te1 = SP_T();
           const int kb = t * kBlock + lrow;
           const uint32_t taddr = tmem + acc * 128 + ((uint32_t)(quad * 32) << 16);
-          uint32_t ua[32], ub[32], uc[32], ud[32];
-          tmem_ld32(taddr, ua);
-          tmem_ld32(taddr + 32, ub);
-          tmem_ld32(taddr + 64, uc);
-          tmem_ld32(taddr + 96, ud);
-          tmem_ld_wait();
-          tc_fence_before();
-          mbar_arrive(acc_empty + acc);  // the accumulator may be overwritten by tile tc + 2
-          const long long te2 = SP_T();
-#define FPB_S(i) __uint_as_float((i) < 32 ? ua[(i)] : (i) < 64 ? ub[(i) - 32] : (i) < 96 ? uc[(i) - 64] : ud[(i) - 96])
-          float mx, s127;
-          if (vr == kBlock) {
-            float m0 = -INFINITY, m1 = -INFINITY;
+          // the 128 scores of this key block, read from TMEM 64 at a time (once for the max,
+          // again for the exponentials)
+          uint32_t ua[32], ub[32];
+          float mx = vr == kBlock ? -INFINITY : 0.f, s127 = 0.f;  // padded rows (q = 0) score 0
 #pragma unroll
-            for (int i = 0; i < 128; i += 4) {
-              m0 = max3(m0, FPB_S(i), FPB_S(i + 1));
-              m1 = max3(m1, FPB_S(i + 2), FPB_S(i + 3));
+          for (int hb = 0; hb < 2; ++hb) {
+            tmem_ld32(taddr + hb * 64, ua);
+            tmem_ld32(taddr + hb * 64 + 32, ub);
+            tmem_ld_wait();
+#define FPB_S(i) __uint_as_float((i) < 32 ? ua[(i)] : ub[(i) - 32])
+            if (vr == kBlock) {
+              float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+              for (int i = 0; i < 64; i += 4) {
+                m0 = max3(m0, FPB_S(i), FPB_S(i + 1));
+                m1 = max3(m1, FPB_S(i + 2), FPB_S(i + 3));
+              }
+              mx = fmaxf(mx, fmaxf(m0, m1));
+              if (hb == 1) s127 = FPB_S(63);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 64; ++i)
+                if (hb * 64 + i < vr) mx = fmaxf(mx, FPB_S(i));
             }
-            mx = fmaxf(m0, m1);
-            s127 = FPB_S(127);
-          } else {  // a sequence's last, partial query block: padded rows have q = 0, s = 0
-            mx = 0.f;
-#pragma unroll
-            for (int i = 0; i < 128; ++i)
-              if (i < vr) mx = fmaxf(mx, FPB_S(i));
-            s127 = 0.f;
+#undef FPB_S
           }
+          const long long te2 = SP_T();
           const bool causal = kb <= qb;
           const bool diag = kb == qb;
           float m = -INFINITY;
@@ -700,30 +709,39 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
           if (any_exp) {
             const float nm = -m;
             float p0 = 0.f, p1 = 0.f;
-            if (vr == kBlock) {
-              // one pair in four on the FMA pipe (exp2_poly2, relative error ~1e-4), the rest
-              // by ex2.approx: the sum only has to resolve the 1e-3 threshold band
 #pragma unroll
-              for (int i = 0; i < 128; i += 2) {
-                float x0, x1, e0, e1;
-                fma2(x0, x1, FPB_S(i), FPB_S(i + 1), c, c, nm, nm);
-                if (((i >> 1) & 3) == 3) {
-                  exp2_poly2(x0, x1, e0, e1);
-                } else {
-                  e0 = ex2_approx(x0);
-                  e1 = ex2_approx(x1);
+            for (int hb = 0; hb < 2; ++hb) {
+              tmem_ld32(taddr + hb * 64, ua);
+              tmem_ld32(taddr + hb * 64 + 32, ub);
+              tmem_ld_wait();
+#define FPB_S(i) __uint_as_float((i) < 32 ? ua[(i)] : ub[(i) - 32])
+              if (vr == kBlock) {
+                // one pair in four on the FMA pipe (exp2_poly2, relative error ~1e-4), the
+                // rest by ex2.approx: the sum only has to resolve the 1e-3 threshold band
+#pragma unroll
+                for (int i = 0; i < 64; i += 2) {
+                  float x0, x1, e0, e1;
+                  fma2(x0, x1, FPB_S(i), FPB_S(i + 1), c, c, nm, nm);
+                  if (((i >> 1) & 3) == 3) {
+                    exp2_poly2(x0, x1, e0, e1);
+                  } else {
+                    e0 = ex2_approx(x0);
+                    e1 = ex2_approx(x1);
+                  }
+                  add2(p0, p1, p0, p1, e0, e1);
                 }
-                add2(p0, p1, p0, p1, e0, e1);
-              }
-              p = p0 + p1;
-            } else {
+              } else {
 #pragma unroll
-              for (int i = 0; i < 128; ++i)
-                if (i < vr) p += ex2_approx(__fmaf_rn(FPB_S(i), c, nm));
-              p += (float)(kBlock - vr) * ex2_approx(-m);
-            }
-          }
+                for (int i = 0; i < 64; ++i)
+                  if (hb * 64 + i < vr) p0 += ex2_approx(__fmaf_rn(FPB_S(i), c, nm));
+              }
 #undef FPB_S
+            }
+            p = p0 + p1;
+            if (vr < kBlock) p += (float)(kBlock - vr) * ex2_approx(-m);
+          }
+          tc_fence_before();
+          mbar_arrive(acc_empty + acc);  // the accumulator may be overwritten by tile tc + 2
           if (diag) p = 1.f;
           if (causal) {
             m_arr[kb] = m;
@@ -745,11 +763,15 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
       ++it;
     }
   } else {
-    // ------------------------------------------------------------ selection (warps 12..15)
+    // ------------------------------------------------------------ selection (warps 12..19)
     regs_dec<kSearchPRoleRegs>();
-    const int es = threadIdx.x - 384;  // 0..127
-    const int wq = warp - 12;
-    uint32_t it = 0, an = 0;
+    const int sg = (warp - 12) >> 2;          // group: array slot sg; fast items alternate too
+    const int es = threadIdx.x - 384 - sg * 128;  // 0..127
+    const int wq = (warp - 12) & 3;
+    float* red = red_all + sg * 4;
+    int* red_i = red_i_all + sg * 4;
+    int* red_k = red_k_all + sg * 4;
+    uint32_t it = 0, an = 0, fn = 0;
     while (true) {
       const int slot = it % kSearchRing;
       if (!SP_TW(kSpSelItem, mbar_wait_warp_sleep(item_full + slot, (it / kSearchRing) & 1, abort))) break;
@@ -762,12 +784,15 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
         int32_t* out_idx = A.idx + ((int64_t)f.h * A.P.tiles_ub + row) * cap;
         int32_t* out_cnt = A.cnt + (int64_t)f.h * A.P.tiles_ub + row;
         if (f.fast) {  // every causal block
-          for (int kb = es; kb <= qb; kb += 128) out_idx[kb] = kb;
-          if (es == 0) *out_cnt = qb + 1;
+          if ((fn++ & 1) == (uint32_t)sg) {
+            for (int kb = es; kb <= qb; kb += 128) out_idx[kb] = kb;
+            if (es == 0) *out_cnt = qb + 1;
+          }
+        } else if ((an++ & 1) != (uint32_t)sg) {
+          // the other group's item
         } else {
-          const int a = an & 1;
-          if (!SP_TW(kSpSelArr, mbar_wait_warp_sleep(arr_full + a, (an >> 1) & 1, abort))) break;
-          ++an;
+          const int a = sg;
+          if (!SP_TW(kSpSelArr, mbar_wait_warp_sleep(arr_full + a, ((an - 1) >> 1) & 1, abort))) break;
           float* m_arr = arr + a * 2 * cap;
           float* p_arr = m_arr + cap;
           uint32_t* marks = marks_all + a * ncw;
@@ -781,12 +806,18 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
             p_arr[kb] = pw;
             best = fmaxf(best, pw);
           }
-          const float thr = __fmul_rn(epi_reduce_max<12, 2>(best, red), A.alpha);
+          // row maximum of pw over the group (named barrier 2 + sg)
+#pragma unroll
+          for (int o = 16; o; o >>= 1) best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, o));
+          named_bar_sync(2 + sg, 128);
+          if (lane == 0) red[wq] = best;
+          named_bar_sync(2 + sg, 128);
+          const float thr = __fmul_rn(fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])), A.alpha);
           const int nwords = (qb + 1 + 31) / 32;
           const int kbudget = min(A.min_budget, qb + 1);
           if (kbudget > 0) {
             for (int wd = es; wd < nwords; wd += 128) marks[wd] = 0u;
-            named_bar_sync(2, 128);
+            named_bar_sync(2 + sg, 128);
           }
           for (int r2 = 0; r2 < kbudget; ++r2) {
             float bv = -INFINITY;
@@ -803,7 +834,7 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
               if (ov > bv || (ov == bv && ok2 < bk)) { bv = ov; bk = ok2; }
             }
             if (lane == 0) { red[wq] = bv; red_k[wq] = bk; }
-            named_bar_sync(2, 128);
+            named_bar_sync(2 + sg, 128);
             if (es == 0) {
               float v0 = red[0];
               int k0 = red_k[0];
@@ -811,7 +842,7 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
                 if (red[j] > v0 || (red[j] == v0 && red_k[j] < k0)) { v0 = red[j]; k0 = red_k[j]; }
               if (k0 <= qb) marks[k0 >> 5] |= 1u << (k0 & 31);
             }
-            named_bar_sync(2, 128);
+            named_bar_sync(2 + sg, 128);
           }
           // selection + ascending compaction: warp wq owns the contiguous key blocks
           // [wq * span, wq * span + span), visited 32 at a time (one per lane, ballot +
@@ -828,7 +859,7 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
           int wcount = 0;
           for (int k0 = w0; k0 < w1; k0 += 32) wcount += __popc(__ballot_sync(0xffffffffu, selected(k0 + lane)));
           if (lane == 0) red_i[wq] = wcount;
-          named_bar_sync(2, 128);
+          named_bar_sync(2 + sg, 128);
           int pre = 0;
           for (int j = 0; j < wq; ++j) pre += red_i[j];
           const int total = red_i[0] + red_i[1] + red_i[2] + red_i[3];
@@ -839,7 +870,7 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
             pre += __popc(bal);
           }
           if (es == 0) *out_cnt = total;
-          named_bar_sync(2, 128);  // every thread has read M, red_i and this item's arrays
+          named_bar_sync(2 + sg, 128);  // every thread has read M, red_i and this item's arrays
           if (es == 0) mrun[a] = float_to_ordered(-INFINITY);
           mbar_arrive(arr_empty + a);
         }
