@@ -273,12 +273,12 @@ def main():
         dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"))
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
-    if w.hk % world:
-        raise SystemExit(f"{w.hk} KV heads do not split over {world} ranks")
-    per = w.hk // world
-    hk0, hk1 = rank * per, (rank + 1) * per
-    G = w.hq // w.hk
-    hq_l, hk_l = per * G, per
+    from flashprefill_b200.sharding import head_shard
+    try:
+        hk0, hk1, hq0, hq1 = head_shard(w.hq, w.hk, rank, world)
+    except ValueError as e:
+        raise SystemExit(str(e))
+    hq_l, hk_l = hq1 - hq0, hk1 - hk0
 
     q, k, v = device_inputs(w, hk0, hk1, dev, seed=w.config_index * 1000 + 1 + hk0)
     T = q.shape[0]
