@@ -46,6 +46,8 @@ def build(force: bool = False, ptxas_verbose: bool = False) -> str:
            "-cudart", "static", "-o", LIB + ".tmp"]
     if ptxas_verbose:
         cmd += ["-Xptxas", "-v"]
+    # extra nvcc flags, e.g. -DFPB_SA_PROFILE=1 for an instrumented build
+    cmd += os.environ.get("FLASHPREFILL_B200_NVCC_FLAGS", "").split()
     cmd += [os.path.join(CSRC, s) for s in SOURCES]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:

@@ -43,6 +43,11 @@ struct AttnArgs {
 };
 
 constexpr int kAttnThreads = 640;
+// One exp2 pair in kPolyEvery is evaluated on the FMA pipe (exp2_poly2), the rest by MUFU.
+#ifndef FPB_POLY_EVERY
+#define FPB_POLY_EVERY 4
+#endif
+constexpr int kPolyEvery = FPB_POLY_EVERY;
 #ifndef FPB_SOFTMAX_PROBE
 #define FPB_SOFTMAX_PROBE 0
 #endif
@@ -528,7 +533,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const int e = ch * 32 + i;
             float x0, x1, p0, p1;
             fma2(x0, x1, __uint_as_float(FPB_U(e)), __uint_as_float(FPB_U(e + 1)), c, c, neg_m, neg_m);
-            if (((i >> 1) & 3) == 3) {
+            if (((i >> 1) % kPolyEvery) == kPolyEvery - 1) {
               exp2_poly2(x0, x1, p0, p1);  // masked (-inf) entries give 2^-126 here, negligible
             } else {
               p0 = ex2_approx(x0);
