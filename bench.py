@@ -196,14 +196,15 @@ def cpu_sample(w, seconds_budget=20.0):
     qpad = np.zeros((nb * 128, G, w.d), np.float32)
     qpad[:L] = qn
     order = np.random.default_rng(0).permutation(nb)
-    done, t_search, sel_rows = 0, 0.0, {}
+    done, t_search, sel_rows, near_rows = 0, 0.0, {}, {}
     while done < nb and t_search < seconds_budget * 0.5:
         chunk = sorted(order[done:done + 16].tolist())
         t1 = time.perf_counter()
         m, p = restate.block_scores_head(qpad[:, 0], mk[:, 0], nb, c, chunk)
         for qb in chunk:
-            s_, _, _ = restate.select_row(m[qb, :qb + 1], p[qb, :qb + 1], qb, nb, w.alpha, 2, 4, 2, True)
+            s_, score, thr = restate.select_row(m[qb, :qb + 1], p[qb, :qb + 1], qb, nb, w.alpha, 2, 4, 2, True)
             sel_rows[qb] = s_
+            near_rows[qb] = np.abs(score - thr) <= 1e-3 * abs(thr)
         t_search += time.perf_counter() - t1
         done += len(chunk)
     sel = np.zeros((1, nb, nb), bool)
@@ -225,8 +226,33 @@ def cpu_sample(w, seconds_budget=20.0):
     info = {"sample": f"KV head 0 + its {G} query heads of one {L}-token sequence: pooled keys of all {nb} "
                       f"blocks, search on {done} random query blocks of one head, attention on {pairs} block "
                       f"pairs; extrapolated to {total_rows} (head, block) rows and E~{int(E_est)} pairs",
-            "cores": os.cpu_count()}
+            "cores": os.cpu_count(),
+            "mask_sample": (q, k, sel_rows, near_rows)}
     return ms, info
+
+
+def mask_exactness(w, sample, dev):
+    """Block sets of the GPU search against the CPU restatement on the sampled rows (same
+    inputs): rows compared, selected blocks, flips inside the 1e-3 threshold band, other flips."""
+    import numpy as np
+
+    import flashprefill_b200 as fp
+
+    q, k, sel_rows, near_rows = sample
+    qd, kd = q.to(dev), k.to(dev)
+    cnt, idx, _, _ = fp.search_dense(qd[None], kd[None], 128, 2, 4, w.alpha, 2, 0)
+    cnt, idx = cnt.cpu().numpy(), idx.cpu().numpy()
+    nb = idx.shape[2]
+    near = other = blocks = 0
+    for qb, ref in sel_rows.items():
+        got = np.zeros(nb, bool)
+        got[idx[0, qb, :cnt[0, qb]]] = True
+        diff = got ^ ref
+        near += int((diff & near_rows[qb]).sum())
+        other += int((diff & ~near_rows[qb]).sum())
+        blocks += int(ref.sum())
+    return {"rows": len(sel_rows), "blocks_selected": blocks, "near_threshold_flips": near, "other_flips": other,
+            "sample": "the CPU baseline's rows (query head 0 of KV head 0, one sequence, same inputs)"}
 
 
 # --------------------------------------------------------------------------- main
@@ -308,8 +334,10 @@ def main():
         step()
     torch.cuda.synchronize()
     fp.check_device_error(ws)
-    cnt = ws[L["cnt"]:L["cnt"] + 4 * hq_l * L["tiles"]].view(torch.int32)
-    E_local = int(cnt.sum().item())
+    # the count rows past the layout's real tiles (varlen reserves an upper bound) are unused
+    cnt = ws[L["cnt"]:L["cnt"] + 4 * hq_l * L["tiles"]].view(torch.int32).view(hq_l, L["tiles"])
+    real_tiles = sum(math.ceil(x / 128) for x in w.seqlens)
+    E_local = int(cnt[:, :real_tiles].sum().item())
 
     # ---- timed region (device-resident inputs)
     evs = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(a.steps)]
@@ -343,42 +371,72 @@ def main():
     if not a.no_e2e:
         hq_, hk_, hv_ = q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()
         hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-        dq, dk, dv, dout = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(out)
+        # Steps are pipelined over three streams (upload, compute, download) with double-buffered
+        # device inputs and outputs: step i's output download (device -> host) overlaps step i+1's
+        # input upload (host -> device) on the full-duplex PCIe link and the compute of either.
+        # Every step still moves all of its inputs in and its whole output out.
+        bufs = [(torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(out))
+                for _ in range(2)]
+        s_in, s_cmp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_cmp = [torch.cuda.Event() for _ in range(2)]
+        ev_out = [torch.cuda.Event() for _ in range(2)]
+        started = [False, False]
 
-        def e2e_step():
-            dq.copy_(hq_, non_blocking=True)
-            dk.copy_(hk_, non_blocking=True)
-            dv.copy_(hv_, non_blocking=True)
-            if w.varlen:
-                fp.flash_prefill_varlen_func(dq, dk, dv, dout, cu, maxlen, w.alpha, 128, 2, 4, 2)
-            else:
-                fp.flash_prefill(dq[None], dk[None], dv[None], dout[None], 128, 2, 4, w.alpha, 2, 0)
-            hout.copy_(dout, non_blocking=True)
+        def e2e_step(i):
+            b = i % 2
+            dq, dk, dv, dout = bufs[b]
+            with torch.cuda.stream(s_in):
+                if started[b]:
+                    s_in.wait_event(ev_cmp[b])  # the compute of step i-2 has read these inputs
+                dq.copy_(hq_, non_blocking=True)
+                dk.copy_(hk_, non_blocking=True)
+                dv.copy_(hv_, non_blocking=True)
+                ev_in[b].record(s_in)
+            with torch.cuda.stream(s_cmp):
+                s_cmp.wait_event(ev_in[b])
+                if started[b]:
+                    s_cmp.wait_event(ev_out[b])  # the download of step i-2 has read this output
+                if w.varlen:
+                    fp.flash_prefill_varlen_func(dq, dk, dv, dout, cu, maxlen, w.alpha, 128, 2, 4, 2)
+                else:
+                    fp.flash_prefill(dq[None], dk[None], dv[None], dout[None], 128, 2, 4, w.alpha, 2, 0)
+                ev_cmp[b].record(s_cmp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_cmp[b])
+                hout.copy_(dout, non_blocking=True)
+                ev_out[b].record(s_out)
+            started[b] = True
 
-        for _ in range(2):
-            e2e_step()
+        for i in range(2):
+            e2e_step(i)
         n_e2e = max(2, min(a.steps, 5))
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s0.record(stream)
-        for _ in range(n_e2e):
-            e2e_step()
-        s1.record(stream)
+        s0.record(s_in)
+        for i in range(2, 2 + n_e2e):
+            e2e_step(i)
+        s_in.wait_stream(s_out)
+        s1.record(s_in)
         torch.cuda.synchronize()
         e2e_ms = torch.tensor([s0.elapsed_time(s1) / n_e2e], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
         e2e = {"value": round(float(e2e_ms), 3), "unit": UNIT,
                "h2d_bytes_per_step": int((q.numel() + k.numel() + v.numel()) * q.element_size() * world),
-               "d2h_bytes_per_step": int(out.numel() * out.element_size() * world), "steps": n_e2e}
+               "d2h_bytes_per_step": int(out.numel() * out.element_size() * world), "steps": n_e2e,
+               "pipelined": "upload / compute / download on three streams, device buffers double-buffered"}
 
     # ---- CPU baseline (rank 0, N=1 only)
     cpu = None
+    exact = None
     if rank == 0 and world == 1 and not a.no_cpu:
         cms, info = cpu_sample(w, seconds_budget=20.0)
         cpu = {"value": round(cms, 3), "unit": UNIT, "cores": info["cores"], "kind": "port", "sample": info["sample"]}
+        if not w.varlen:
+            exact = mask_exactness(w, info["mask_sample"], dev)
 
     if rank != 0:
         if world > 1:
@@ -409,6 +467,7 @@ def main():
             "search_ms": round(t_s, 4), "attention_ms": round(t_a, 4),
             "executed_pairs": E_total, "density": round(E_total / P_pairs, 5),
             "roofline": roof, "roofline_search": roof_s, "e2e": e2e, "cpu_baseline": cpu,
+            "mask_exactness": exact,
             "gpu_launches": a.steps * (3 + (1 if w.varlen else 0)),
             "clocks": clocks, "wall_s_timed": round(t_wall, 3)}
     print(json.dumps(line))
