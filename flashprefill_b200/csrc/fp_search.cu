@@ -419,11 +419,13 @@ constexpr int kSearchPThreads = 640;
 constexpr int kSearchPLaunchRegs = 96, kSearchPRoleRegs = 64, kSearchPEpiRegs = 144;
 static_assert(384 * kSearchPRoleRegs + 256 * kSearchPEpiRegs <= kSearchPThreads * kSearchPLaunchRegs, "split");
 constexpr int kSearchRing = 4;
-constexpr int kSearchMaxCap = 4096;
+constexpr int kSearchMaxCap = 2048;
+constexpr int kSearchStages = 4;  // pooled-key tiles in flight and TMEM accumulators (2 per epilogue group)
 
 __host__ __device__ constexpr size_t search_p_smem_bytes(int cap) {
-  // Q x2, pooled keys x2, two item slots of (m, p, top-k marks), barriers / ring, alignment
-  return 4 * (size_t)kTileBytes + 2 * (8 * (size_t)cap + (size_t)((cap + 31) / 32) * 4) + 1024 + 1024;
+  // Q x2, pooled keys x4, two item slots of (m, p, top-k marks), barriers / ring, alignment
+  return (2 + kSearchStages) * (size_t)kTileBytes + 2 * (8 * (size_t)cap + (size_t)((cap + 31) / 32) * 4) + 1024 +
+         1024;
 }
 
 // Tiles of a row are visited last first (diagonal and window blocks), then from the first
@@ -464,10 +466,10 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                   // [2]
-  uint8_t* sMK = smem + 2 * kTileBytes;  // [2]
+  uint8_t* sMK = smem + 2 * kTileBytes;  // [stages]
   const int cap = A.P.cap;
   const int ncw = (cap + 31) / 32;
-  float* arr = reinterpret_cast<float*>(smem + 4 * kTileBytes);      // [2]{m[cap], p[cap]}
+  float* arr = reinterpret_cast<float*>(smem + (2 + kSearchStages) * kTileBytes);  // [2]{m[cap], p[cap]}
   uint32_t* marks_all = reinterpret_cast<uint32_t*>(arr + 4 * cap);  // [2][ncw]
   uint8_t* misc = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(marks_all + 2 * ncw) + 15) & ~uintptr_t(15));
@@ -476,15 +478,15 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
   uint64_t* item_empty = bars + 4;   // [ring]
   uint64_t* q_full = bars + 8;       // [2]
   uint64_t* q_empty = bars + 10;     // [2]
-  uint64_t* mk_full = bars + 12;     // [2]
-  uint64_t* mk_empty = bars + 14;    // [2]
-  uint64_t* acc_full = bars + 16;    // [2]
-  uint64_t* acc_empty = bars + 18;   // [2]
-  uint64_t* arr_full = bars + 20;    // [2] an item's m / p complete
-  uint64_t* arr_empty = bars + 22;   // [2] an item's m / p consumed
-  uint64_t* mma_done = bars + 24;
-  SearchItem* ring = reinterpret_cast<SearchItem*>(misc + 256);  // [ring]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 512);
+  uint64_t* arr_full = bars + 12;    // [2] an item's m / p complete
+  uint64_t* arr_empty = bars + 14;   // [2] an item's m / p consumed
+  uint64_t* mma_done = bars + 16;
+  uint64_t* mk_full = bars + 17;     // [stages]
+  uint64_t* mk_empty = bars + 21;    // [stages]
+  uint64_t* acc_full = bars + 25;    // [stages]
+  uint64_t* acc_empty = bars + 29;   // [stages]
+  SearchItem* ring = reinterpret_cast<SearchItem*>(misc + 512);  // [ring]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 768);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* mrun = reinterpret_cast<int*>(tmem_slot + 2);     // [2] running max per item slot (ordered int)
   float* red_all = reinterpret_cast<float*>(tmem_slot + 4);  // [2 groups][4] selection reductions
@@ -500,20 +502,22 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(q_full + i, 1);
       mbar_init(q_empty + i, 1);
+      mbar_init(arr_full + i, 256);
+      mbar_init(arr_empty + i, 128);
+      mrun[i] = float_to_ordered(-INFINITY);
+    }
+    for (int i = 0; i < kSearchStages; ++i) {
       mbar_init(mk_full + i, 1);
       mbar_init(mk_empty + i, 1);
       mbar_init(acc_full + i, 1);
       mbar_init(acc_empty + i, 128);
-      mbar_init(arr_full + i, 256);
-      mbar_init(arr_empty + i, 128);
-      mrun[i] = float_to_ordered(-INFINITY);
     }
     mbar_init(mma_done, 1);
     *abort = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -570,8 +574,11 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
         const int hk = f.h / group, ntiles = f.qb / kBlock + 1;
         for (int j = 0; j < ntiles; ++j, ++tn) {
           const int t = tile_order(j, ntiles);
-          const int st = tn & 1;
-          if (!SP_TW(kSpProdMk, mbar_wait_sleep(mk_empty + st, ((tn >> 1) & 1) ^ 1, abort))) { ok = false; break; }
+          const int st = tn % kSearchStages;
+          if (!SP_TW(kSpProdMk, mbar_wait_sleep(mk_empty + st, ((tn / kSearchStages) & 1) ^ 1, abort))) {
+            ok = false;
+            break;
+          }
           mbar_arrive_expect_tx(mk_full + st, kTileBytes);
           uint8_t* dst = sMK + st * kTileBytes;
           const int mrow = f.tile_base + t * kBlock;
@@ -606,9 +613,10 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
           const uint32_t q_base = smem_u32(sQ + qs * kTileBytes);
           const int ntiles = f.qb / kBlock + 1;
           for (int t = 0; t < ntiles; ++t, ++tc) {
-            const int st = tc & 1;
-            if (!SP_TW(kSpMmaMk, mbar_wait(mk_full + st, (tc >> 1) & 1, abort))) { ok = false; break; }
-            if (!SP_TW(kSpMmaAcc, mbar_wait(acc_empty + st, ((tc >> 1) & 1) ^ 1, abort))) { ok = false; break; }
+            const int st = tc % kSearchStages;  // pooled-key stage = accumulator
+            const uint32_t ph = (tc / kSearchStages) & 1;
+            if (!SP_TW(kSpMmaMk, mbar_wait(mk_full + st, ph, abort))) { ok = false; break; }
+            if (!SP_TW(kSpMmaAcc, mbar_wait(acc_empty + st, ph ^ 1, abort))) { ok = false; break; }
             tc_fence_after();
             const uint32_t a_base = smem_u32(sMK + st * kTileBytes);
 #pragma unroll
@@ -659,9 +667,12 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
         const int ntiles = qb / kBlock + 1;
         for (int j = 0; j < ntiles; ++j, ++tc) {
           const int t = tile_order(j, ntiles);
-          const int acc = tc & 1;
-          if (acc != eg) continue;  // the other group's tile
-          if (!SP_TW(kSpEpiAcc, mbar_wait_warp_sleep(acc_full + acc, (tc >> 1) & 1, abort))) { ok = false; break; }
+          if ((int)(tc & 1) != eg) continue;  // the other group's tile
+          const int acc = tc % kSearchStages;
+          if (!SP_TW(kSpEpiAcc, mbar_wait_warp_sleep(acc_full + acc, (tc / kSearchStages) & 1, abort))) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           const long long te1 = SP_T();
           const int kb = t * kBlock + lrow;
@@ -896,7 +907,7 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
   if (threadIdx.x == 0 && *abort) raise_error(A.P.err, kErrWaitTimeout);
 }
