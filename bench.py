@@ -265,11 +265,14 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--shard", default=None, help="R/N: run rank R's share of an N-GPU job alone on one GPU "
+                    "(no process group; for studying the per-rank work)")
     a = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    shard = tuple(int(x) for x in a.shard.split("/")) if a.shard else None
     w = workload(a.workload)
 
     if a.impl == "reference":
@@ -301,7 +304,7 @@ def main():
     dev = torch.device(f"cuda:{local}")
     from flashprefill_b200.sharding import head_shard
     try:
-        hk0, hk1, hq0, hq1 = head_shard(w.hq, w.hk, rank, world)
+        hk0, hk1, hq0, hq1 = head_shard(w.hq, w.hk, *(shard if shard else (rank, world)))
     except ValueError as e:
         raise SystemExit(str(e))
     hq_l, hk_l = hq1 - hq0, hk1 - hk0

@@ -56,6 +56,10 @@ int fail(int code, const char* fmt, ...) {
 struct Layout {
   int64_t err, cu_tile, mk, cnt, idx, total;
   int tiles, cap;
+  // Optional tail (long rows split into chunks, fp_split.cu): used when the caller's workspace
+  // reaches total_split; base_total is the required minimum.
+  int64_t base_total, sp_head, sp_entries, sp_rowidx, sp_counters, sp_part, total_split;
+  int max_chunks, max_split_rows;
 };
 
 int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
@@ -84,7 +88,24 @@ Layout make_layout(int varlen, int a, int b, int c, int hq, int hk) {
   off = align256(off + 4 * (int64_t)hq * L.tiles);
   L.idx = off;
   off = align256(off + 4 * (int64_t)hq * L.tiles * L.cap);
-  L.total = off;
+  L.base_total = off;
+  // split region: enough chunks for two full-length rows per sequence and head (the last-N
+  // band at its default width) plus a quarter more; further long rows stay whole
+  const int chunks_per_row = (L.cap + kSplitChunk - 1) / kSplitChunk;
+  L.max_chunks = L.cap > kSplitChunk ? (int)std::min<int64_t>(2LL * nseq * hq * chunks_per_row * 5 / 4, 1 << 16) : 0;
+  L.max_split_rows = L.max_chunks;
+  L.sp_head = off;
+  off = align256(off + 256);
+  L.sp_entries = off;
+  off = align256(off + 16 * (int64_t)L.max_chunks);
+  L.sp_rowidx = off;
+  off = align256(off + 4 * (int64_t)hq * L.tiles);
+  L.sp_counters = off;
+  off = align256(off + 4 * (int64_t)L.max_split_rows);
+  L.sp_part = off;
+  off = align256(off + kSplitPartBytes * L.max_chunks);
+  L.total_split = L.max_chunks > 0 ? off : L.base_total;
+  L.total = L.total_split;  // what callers should allocate
   return L;
 }
 
@@ -316,7 +337,7 @@ int run_search(const Geometry& g, const void* q, const void* k, const int64_t qs
 
 int run_attention(const Geometry& g, const void* q, const void* k, const void* v, void* o, const int64_t qs[3],
                   const int64_t ks[3], const int64_t vs[3], const int64_t os[3], uint8_t* ws, const Layout& L,
-                  cudaStream_t stream) {
+                  size_t ws_bytes, cudaStream_t stream) {
   SeqProblem P = make_problem(g, L, ws);
   const int rows = g.varlen ? g.total_tokens : g.seqlen;
   const int batch = g.varlen ? 1 : g.batch;
@@ -337,6 +358,28 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
   A.o_sb = os[0];
   A.o_ss = os[1];
   A.o_sh = os[2];
+  // long rows as parallel chunks when the workspace holds the split area
+  A.split = L.max_chunks > 0 && (int64_t)ws_bytes >= L.total_split && std::getenv("FLASHPREFILL_B200_NO_SPLIT") == nullptr;
+  if (A.split) {
+    SplitArgs S{};
+    S.P = P;
+    S.cnt = A.cnt;
+    S.total_items = A.total_items;
+    S.max_chunks = L.max_chunks;
+    S.max_rows = L.max_split_rows;
+    S.entries = reinterpret_cast<SplitEntry*>(ws + L.sp_entries);
+    S.head = reinterpret_cast<int*>(ws + L.sp_head);
+    S.rowidx = reinterpret_cast<int*>(ws + L.sp_rowidx);
+    S.counters = reinterpret_cast<int*>(ws + L.sp_counters);
+    FPB_CUDA(cudaMemsetAsync(S.head, 0, 16, stream));
+    split_plan_kernel<<<1, kPlanThreads, 0, stream>>>(S);
+    FPB_CUDA(cudaGetLastError());
+    A.sp_entries = S.entries;
+    A.sp_head = S.head;
+    A.sp_rowidx = S.rowidx;
+    A.sp_counters = S.counters;
+    A.sp_part = reinterpret_cast<float*>(ws + L.sp_part);
+  }
   A.profile = std::getenv("FLASHPREFILL_B200_PROFILE") != nullptr;
   A.alt_issue = std::getenv("FLASHPREFILL_B200_ISSUE") && std::strcmp(std::getenv("FLASHPREFILL_B200_ISSUE"), "alt") == 0;
   A.trace = std::getenv("FLASHPREFILL_B200_TRACE") != nullptr;
@@ -440,8 +483,8 @@ int check_varlen_vo(const void* v, const void* o, const int64_t* vs, const int64
 int check_ws(const void* ws, size_t bytes, const Layout& L) {
   FPB_CHECK_ARG(ws != nullptr && (reinterpret_cast<uintptr_t>(ws) & 255) == 0,
                 "workspace must be a 256-byte aligned device pointer");
-  FPB_CHECK_ARG((int64_t)bytes >= L.total, "workspace too small: %zu bytes given, %lld needed", bytes,
-                (long long)L.total);
+  FPB_CHECK_ARG((int64_t)bytes >= L.base_total, "workspace too small: %zu bytes given, %lld needed", bytes,
+                (long long)L.base_total);
   return FPB_OK;
 }
 
@@ -529,7 +572,7 @@ int fpb_attention_dense(const void* q, const void* k, const void* v, void* out, 
   FPB_TRY(check_ws(workspace, workspace_bytes, L));
   Geometry g{0, batch, seqlen, 0, 0, batch, hq, hk, dtype, nullptr};
   return run_attention(g, q, k, v, out, q_strides, k_strides, v_strides, o_strides, static_cast<uint8_t*>(workspace),
-                       L, static_cast<cudaStream_t>(stream));
+                       L, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int fpb_attention_varlen(const void* q, const void* k, const void* v, void* o, int dtype, const int32_t* cu_seqlens,
@@ -549,7 +592,7 @@ int fpb_attention_varlen(const void* q, const void* k, const void* v, void* o, i
   s3(k_strides, ks);
   s3(v_strides, vs);
   s3(o_strides, os);
-  return run_attention(g, q, k, v, o, qs, ks, vs, os, static_cast<uint8_t*>(workspace), L,
+  return run_attention(g, q, k, v, o, qs, ks, vs, os, static_cast<uint8_t*>(workspace), L, workspace_bytes,
                        static_cast<cudaStream_t>(stream));
 }
 
@@ -567,7 +610,7 @@ int fpb_prefill_dense(const void* q, const void* k, const void* v, void* out, in
   auto st = static_cast<cudaStream_t>(stream);
   FPB_TRY(run_search(g, q, k, q_strides, k_strides, attention_sink, window_size, alpha, last_n_block_full, min_budget,
                      mean_model, ws, L, st));
-  return run_attention(g, q, k, v, out, q_strides, k_strides, v_strides, o_strides, ws, L, st);
+  return run_attention(g, q, k, v, out, q_strides, k_strides, v_strides, o_strides, ws, L, workspace_bytes, st);
 }
 
 int fpb_prefill_varlen(const void* q, const void* k, const void* v, void* o, int dtype, const int32_t* cu_seqlens,
@@ -590,7 +633,7 @@ int fpb_prefill_varlen(const void* q, const void* k, const void* v, void* o, int
   auto* ws = static_cast<uint8_t*>(workspace);
   auto st = static_cast<cudaStream_t>(stream);
   FPB_TRY(run_search(g, q, k, qs, ks, attention_sink, window_size, alpha, last_n_block, 0, mean_model, ws, L, st));
-  return run_attention(g, q, k, v, o, qs, ks, vs, os, ws, L, st);
+  return run_attention(g, q, k, v, o, qs, ks, vs, os, ws, L, workspace_bytes, st);
 }
 
 int fpb_read_device_error(const void* workspace, uint32_t* flags, void* stream) {

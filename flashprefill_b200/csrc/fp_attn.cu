@@ -25,6 +25,7 @@
 // The largest P of a row is exactly 1.0, which keeps the bf16 rounding of P at the
 // reference's level (a lazy max that lets P grow above 1 adds up to one bf16 ulp of P).
 #include "fp_common.cuh"
+#include "fp_split.cu"
 
 namespace fpb {
 
@@ -40,6 +41,13 @@ struct AttnArgs {
   int total_items;           // tiles_ub * hq
   void* out;                 // output base (masked-store path)
   int64_t o_sb, o_ss, o_sh;  // output strides in elements
+  // long rows split into chunks (fp_split.cu); split = 0 processes every row whole
+  int split;
+  const SplitEntry* sp_entries;
+  const int* sp_head;        // [0] chunk entries
+  const int* sp_rowidx;      // [hq][tiles_ub] split-row index or -1
+  int* sp_counters;          // per split row: chunks finished
+  float* sp_part;            // per chunk entry: O [128][128], m [128], l [2][128]
 };
 
 constexpr int kAttnThreads = 640;
@@ -96,13 +104,17 @@ constexpr uint32_t kAttnTile = 128 * 128 * 2;
 constexpr uint32_t kAttnHalf = kAttnTile / 2;
 
 // 6 tiles, alignment slack, barriers / item ring / counters, row max and sum exchange (6 KB)
-__host__ __device__ constexpr size_t attn_smem_bytes() { return (size_t)kAttnTile * 6 + 1024 + 1024 + 6144; }
+__host__ __device__ constexpr size_t attn_smem_bytes() { return (size_t)kAttnTile * 6 + 1024 + 1024 + 6400; }
 
 // One work item as published by a pipeline's scheduler in its smem ring.
 struct ItemInfo {
   int valid;  // 0: no more work, 1: item, 2: empty slot of the grid (skip)
   int start, len, tile_base, bcoord, qb, h, n, last_kb;
-  int pad[7];
+  int j0;       // first list entry of this item (a chunk of a split row; 0 otherwise)
+  int entry;    // chunk entry (partial-result slot) or -1 for a whole row
+  int nchunks;  // chunks of the split row
+  int srow;     // split-row index (completion counter)
+  int pad[3];
 };
 
 template <typename T>
@@ -193,6 +205,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     prefetch_tmap(&tm_v);
     const uint64_t stream_once = l2_policy_evict_first();
     uint32_t it = 0, kseq = 0, vseq = 0, qld = 0, sfc = 0;
+    // chunks of split rows come first in the work order (they are the longest work)
+    const int n_ent = A.split ? *A.sp_head : 0;
     bool ok = true;
     while (ok) {
       const int slot = it & 1;
@@ -200,12 +214,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       ItemInfo f{};
       const int id = atomicAdd(A.counter, 1);
       const int32_t* lst = nullptr;
-      if (id >= A.total_items) {
+      if (id >= n_ent + A.total_items) {
         f.valid = 0;
       } else {
         SeqInfo s;
         int qb;
-        const int tile = id / A.P.hq, h = id - tile * A.P.hq;
+        const SplitEntry se = id < n_ent ? A.sp_entries[id] : SplitEntry{id - n_ent, 0, 0, -1};
+        const int tile = se.item / A.P.hq, h = se.item - tile * A.P.hq;
         if (!decode_item(A.P, tile, s, qb)) {
           f.valid = 2;
         } else {
@@ -217,8 +232,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           f.qb = qb;
           f.h = h;
           const int64_t row = (int64_t)f.h * A.P.tiles_ub + s.tile_base + qb;
-          f.n = max(0, min(__ldg(A.cnt + row), qb + 1));
-          lst = A.idx + row * A.P.cap;
+          const int n_row = max(0, min(__ldg(A.cnt + row), qb + 1));
+          f.entry = -1;
+          if (id < n_ent) {  // one chunk of a split row
+            f.j0 = se.chunk * kSplitChunk;
+            f.n = min(kSplitChunk, n_row - f.j0);
+            f.entry = id;
+            f.nchunks = se.nchunks;
+            f.srow = se.srow;
+          } else {
+            f.n = n_row;
+            if (A.split && __ldg(A.sp_rowidx + row) >= 0) f.valid = 2;  // done as chunks
+          }
+          lst = A.idx + row * A.P.cap + f.j0;
           f.last_kb = f.n > 0 ? __ldg(lst + f.n - 1) : -1;
         }
       }
@@ -445,6 +471,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t t_o = tmem + 256 + x * 128 + lane_off + hh * 64;
     float* xch = xchg + x * 512;                // row max: [parity][half][row]
     float* xl = xchg + 1024 + x * 256;          // row sum: [half][row]
+    int* last_chunk = reinterpret_cast<int*>(xchg + 1536) + x;  // this pipeline finished a split row
     const float c = A.c;
     const bool rec = tr && r == 0 && hh == 0;
     uint32_t it = 0, sc = 0, oc = 0, ep = 0, mp = 0;
@@ -585,6 +612,67 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(o_empty + x);  // O_x may be overwritten by the next item's first PV
+      if (f.entry >= 0) {
+        // a chunk of a split row: store its unnormalised O, m and l; the last chunk of the
+        // row to finish merges all of them into the output
+        const int et = hh * 128 + r;
+        float* part = A.sp_part + (int64_t)f.entry * (kSplitPartBytes / 4);
+        float4* po = reinterpret_cast<float4*>(part + r * 128 + hh * 64);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          po[i] = make_float4(__uint_as_float(oa[4 * i]), __uint_as_float(oa[4 * i + 1]), __uint_as_float(oa[4 * i + 2]),
+                              __uint_as_float(oa[4 * i + 3]));
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          po[8 + i] = make_float4(__uint_as_float(ob[4 * i]), __uint_as_float(ob[4 * i + 1]),
+                                  __uint_as_float(ob[4 * i + 2]), __uint_as_float(ob[4 * i + 3]));
+        if (hh == 0) part[128 * 128 + r] = m_use;
+        part[128 * 128 + 128 + hh * 128 + r] = l;
+        __threadfence();
+        if (!group_sync()) break;
+        if (et == 0) *last_chunk = atomicAdd(A.sp_counters + f.srow, 1) == f.nchunks - 1;
+        if (!group_sync()) break;
+        if (*(volatile int*)last_chunk) {
+          __threadfence();
+          const float* p0 = A.sp_part + (int64_t)(f.entry - f.j0 / kSplitChunk) * (kSplitPartBytes / 4);
+          float M = -INFINITY;
+          for (int cix = 0; cix < f.nchunks; ++cix)
+            M = fmaxf(M, __ldcg(p0 + (int64_t)cix * (kSplitPartBytes / 4) + 128 * 128 + r));
+          float acc[64];
+#pragma unroll
+          for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+          float Lsum = 0.f;
+          for (int cix = 0; cix < f.nchunks; ++cix) {
+            const float* pc = p0 + (int64_t)cix * (kSplitPartBytes / 4);
+            const float sc = ex2_approx(__ldcg(pc + 128 * 128 + r) - M);
+            Lsum += (__ldcg(pc + 128 * 128 + 128 + r) + __ldcg(pc + 128 * 128 + 256 + r)) * sc;
+            const float4* src = reinterpret_cast<const float4*>(pc + r * 128 + hh * 64);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float4 v4 = __ldcg(src + i);
+              acc[4 * i] += v4.x * sc;
+              acc[4 * i + 1] += v4.y * sc;
+              acc[4 * i + 2] += v4.z * sc;
+              acc[4 * i + 3] += v4.w * sc;
+            }
+          }
+          const float invL = 1.f / Lsum;
+          if (r < vr) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + (int64_t)r * A.o_ss + hh * 64);
+#pragma unroll
+            for (int q4 = 0; q4 < 8; ++q4) {
+              uint32_t pk[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                pk[i] = DT<T>::pack(acc[q4 * 8 + 2 * i] * invL, acc[q4 * 8 + 2 * i + 1] * invL);
+              dst[q4] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            }
+          }
+        }
+        if (et == 0) mbar_arrive(stage_free + x);  // the V tile was not used for staging
+        pa.add(11, clk() - te0);
+        continue;
+      }
       if (!group_sync()) break;
       const float inv = 1.f / (l + xl[(hh ^ 1) * 128 + r]);
       uint8_t* stage = smem + x * 3 * kAttnTile + 2 * kAttnTile;  // V tile: its last PV has completed

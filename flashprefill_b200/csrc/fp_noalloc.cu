@@ -54,9 +54,11 @@ extern "C" int fpb_prefill_dense_noalloc(const void* q, const void* k, const voi
   using namespace fpb;
   FPB_CHECK_ARG(batch >= 1 && seqlen >= 1 && hq >= 1 && hk >= 1, "batch, seqlen and head counts must be >= 1");
   const Layout L = make_layout(0, batch, seqlen, 0, hq, hk);
-  FPB_CHECK_ARG((size_t)L.total <= kNoAllocScratchBytes,
+  // the required part of the workspace must fit; the optional long-row split area is used
+  // only where it fits as well
+  FPB_CHECK_ARG((size_t)L.base_total <= kNoAllocScratchBytes,
                 "problem needs %lld bytes of scratch; the no-allocation path holds at most %zu (32 MiB) -- use "
-                "fpb_prefill_dense with a caller workspace", (long long)L.total, kNoAllocScratchBytes);
+                "fpb_prefill_dense with a caller workspace", (long long)L.base_total, kNoAllocScratchBytes);
   void* ws = nullptr;
   FPB_TRY(noalloc_scratch(&ws));
   return fpb_prefill_dense(q, k, v, out, dtype, batch, seqlen, hq, hk, head_dim, q_strides, k_strides, v_strides,

@@ -166,3 +166,46 @@ def test_bad_cu_seqlens_reported_on_device():
     ws = _ops.prefill_varlen(qd, kd, vd, o, cud, 512, 0.1)
     with pytest.raises(fp.FlashPrefillError, match="cu_seqlens"):
         fp.check_device_error(ws)
+
+
+@pytest.mark.parametrize("lens,varlen", [([20000], False), ([20000, 3000], True)])
+def test_split_long_rows_match_oracle(lens, varlen, monkeypatch):
+    """Rows longer than 64 listed blocks (here the last-N rows, 157 blocks) are processed as
+    parallel chunks whose partial results are merged; their output must match the fp32
+    recomputation like every other row, with and without the split."""
+    hq, hk, alpha, dtype = 4, 1, 0.05, torch.bfloat16
+    q, k, v, cu = gu.make_packed(lens, hq, hk, dtype, seed0=sum(lens) + 7)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    cud = torch.tensor(cu, dtype=torch.int32, device=DEV)
+    if varlen:
+        cnt, idx, _, _, ws = fp.search_varlen(qd, kd, cud, max(lens), alpha, 128, 2, 4, 2)
+    else:
+        cnt, idx, _, ws = fp.search_dense(qd[None], kd[None], 128, 2, 4, alpha, 2, 0)
+    gmasks = gu.lists_to_masks(cnt, idx, cu, hq)
+    layout, _ = restate.seq_layout(cu)
+    rng = np.random.default_rng(0)
+    rows = set()
+    for si, (_, _, nb, _) in enumerate(layout):
+        for h in range(hq):
+            for qb in [nb - 1, nb - 2] + list(rng.integers(0, nb, 3)):
+                rows.add((si, h, int(qb)))
+    assert max(int(m.sum(-1).max()) for m in gmasks) > 64, "the case must contain rows to split"
+    ref = gu.ref_attention_rows(q, k, v, cu, gmasks, hq, hk, rows=rows)
+    sel = np.zeros(ref.shape[:2], bool)
+    for si, h, qb in rows:
+        start, L, _, _ = layout[si]
+        sel[start + qb * 128:start + min(L, (qb + 1) * 128), h] = True
+    for split in (True, False):
+        if split:
+            monkeypatch.delenv("FLASHPREFILL_B200_NO_SPLIT", raising=False)
+        else:
+            monkeypatch.setenv("FLASHPREFILL_B200_NO_SPLIT", "1")
+        o = torch.zeros_like(qd)
+        if varlen:
+            fp.flash_prefill_varlen_func(qd, kd, vd, o, cud, max(lens), alpha, 128, 2, 4, 2)
+        else:
+            fp.flash_prefill(qd[None], kd[None], vd[None], o[None], 128, 2, 4, alpha, 2, 0)
+        torch.cuda.synchronize()
+        err = np.abs(o.float().cpu().numpy() - ref)[sel]
+        print(f"  split={split} rows={len(rows)} max-abs {err.max():.3e} mean-abs {err.mean():.3e}")
+        assert err.max() <= gu.MAX_ABS and err.mean() <= gu.MEAN_ABS
