@@ -95,7 +95,7 @@ Layout make_layout(int varlen, int a, int b, int c, int hq, int hk) {
   L.max_chunks = L.cap > kSplitChunk ? (int)std::min<int64_t>(2LL * nseq * hq * chunks_per_row * 5 / 4, 1 << 16) : 0;
   L.max_split_rows = L.max_chunks;
   L.sp_head = off;
-  off = align256(off + 256);
+  off = align256(off + kPlanHeadBytes);
   L.sp_entries = off;
   off = align256(off + 16 * (int64_t)L.max_chunks);
   L.sp_rowidx = off;
@@ -337,7 +337,7 @@ int run_search(const Geometry& g, const void* q, const void* k, const int64_t qs
 
 int run_attention(const Geometry& g, const void* q, const void* k, const void* v, void* o, const int64_t qs[3],
                   const int64_t ks[3], const int64_t vs[3], const int64_t os[3], uint8_t* ws, const Layout& L,
-                  size_t ws_bytes, cudaStream_t stream) {
+                  size_t ws_bytes, cudaStream_t stream, int64_t listed_lower_bound = 0) {
   SeqProblem P = make_problem(g, L, ws);
   const int rows = g.varlen ? g.total_tokens : g.seqlen;
   const int batch = g.varlen ? 1 : g.batch;
@@ -358,20 +358,30 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
   A.o_sb = os[0];
   A.o_ss = os[1];
   A.o_sh = os[2];
+  int sms = 0;
+  FPB_TRY(sm_count(&sms));
+  const unsigned grid = (unsigned)std::min(sms, A.total_items);
   // long rows as parallel chunks when the workspace holds the split area
   A.split = L.max_chunks > 0 && (int64_t)ws_bytes >= L.total_split && std::getenv("FLASHPREFILL_B200_NO_SPLIT") == nullptr;
+  // No row can pass the plan's threshold if even the longest possible row is within it for
+  // the fewest blocks the lists can hold: then the plan is not run at all.
+  if (A.split && listed_lower_bound > 0 &&
+      (int64_t)std::min(L.cap, ((g.varlen ? g.max_seq_len : g.seqlen) + kBlock - 1) / kBlock) * kSplitThrDen * 2 * (int64_t)grid <=
+          listed_lower_bound * kSplitThrNum)
+    A.split = 0;
   if (A.split) {
     SplitArgs S{};
     S.P = P;
     S.cnt = A.cnt;
     S.total_items = A.total_items;
     S.max_chunks = L.max_chunks;
-    S.max_rows = L.max_split_rows;
+    S.pipelines = 2 * (int)grid;
     S.entries = reinterpret_cast<SplitEntry*>(ws + L.sp_entries);
     S.head = reinterpret_cast<int*>(ws + L.sp_head);
     S.rowidx = reinterpret_cast<int*>(ws + L.sp_rowidx);
     S.counters = reinterpret_cast<int*>(ws + L.sp_counters);
-    FPB_CUDA(cudaMemsetAsync(S.head, 0, 16, stream));
+    FPB_CUDA(cudaMemsetAsync(S.head, 0, kPlanHeadClear, stream));
+    split_scan_kernel<<<(unsigned)((A.total_items + kScanThreads - 1) / kScanThreads), kScanThreads, 0, stream>>>(S);
     split_plan_kernel<<<1, kPlanThreads, 0, stream>>>(S);
     FPB_CUDA(cudaGetLastError());
     A.sp_entries = S.entries;
@@ -400,9 +410,6 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
                   fa.numRegs, kAttnLaunchRegs);
   }
   const size_t smem = attn_smem_bytes();
-  int sms = 0;
-  FPB_TRY(sm_count(&sms));
-  const unsigned grid = (unsigned)std::min(sms, A.total_items);
   if (g.dtype == FPB_BF16) {
     FPB_TRY(set_smem(sparse_attn_kernel<__nv_bfloat16>, smem));
     sparse_attn_kernel<__nv_bfloat16><<<grid, kAttnThreads, smem, stream>>>(tm_q, tm_k, tm_v, tm_o, A);
@@ -596,6 +603,22 @@ int fpb_attention_varlen(const void* q, const void* k, const void* v, void* o, i
                        static_cast<cudaStream_t>(stream));
 }
 
+// Fewest listed blocks a dense search can return: its lists hold at least the structural
+// blocks of every row (sinks, the local window, and whole rows for the last-N query blocks).
+int64_t dense_listed_lower_bound(int batch, int seqlen, int hq, int sink, int window, int last_n) {
+  const int64_t nb = (seqlen + kBlock - 1) / kBlock;
+  int64_t per_head = 0;
+  for (int64_t qb = 0; qb < nb; ++qb)
+    if (qb >= nb - last_n) {
+      per_head += qb + 1;
+    } else {  // |[0, sink) U (qb - window, qb]| within [0, qb]
+      const int64_t s_end = std::min<int64_t>(std::max(sink, 0), qb + 1), w_lo = std::max<int64_t>(0, qb - window + 1);
+      const int64_t w_n = window > 0 ? qb + 1 - w_lo : 0;
+      per_head += s_end + w_n - (window > 0 ? std::max<int64_t>(0, s_end - w_lo) : 0);
+    }
+  return per_head * hq * batch;
+}
+
 int fpb_prefill_dense(const void* q, const void* k, const void* v, void* out, int dtype, int batch, int seqlen,
                       int hq, int hk, int head_dim, const int64_t* q_strides, const int64_t* k_strides,
                       const int64_t* v_strides, const int64_t* o_strides, int block_size, int attention_sink,
@@ -610,7 +633,8 @@ int fpb_prefill_dense(const void* q, const void* k, const void* v, void* out, in
   auto st = static_cast<cudaStream_t>(stream);
   FPB_TRY(run_search(g, q, k, q_strides, k_strides, attention_sink, window_size, alpha, last_n_block_full, min_budget,
                      mean_model, ws, L, st));
-  return run_attention(g, q, k, v, out, q_strides, k_strides, v_strides, o_strides, ws, L, workspace_bytes, st);
+  return run_attention(g, q, k, v, out, q_strides, k_strides, v_strides, o_strides, ws, L, workspace_bytes, st,
+                       dense_listed_lower_bound(batch, seqlen, hq, attention_sink, window_size, last_n_block_full));
 }
 
 int fpb_prefill_varlen(const void* q, const void* k, const void* v, void* o, int dtype, const int32_t* cu_seqlens,

@@ -44,9 +44,9 @@ struct AttnArgs {
   // long rows split into chunks (fp_split.cu); split = 0 processes every row whole
   int split;
   const SplitEntry* sp_entries;
-  const int* sp_head;        // [0] chunk entries
-  const int* sp_rowidx;      // [hq][tiles_ub] split-row index or -1
-  int* sp_counters;          // per split row: chunks finished
+  const int* sp_head;        // plan header: [0] chunk entries, [3] split threshold
+  const int* sp_rowidx;      // [hq][tiles_ub] split-row index or -1 (rows over the threshold)
+  int* sp_counters;          // chunks finished per split row, at the row's first entry
   float* sp_part;            // per chunk entry: O [128][128], m [128], l [2][128]
 };
 
@@ -110,12 +110,106 @@ __host__ __device__ constexpr size_t attn_smem_bytes() { return (size_t)kAttnTil
 struct ItemInfo {
   int valid;  // 0: no more work, 1: item, 2: empty slot of the grid (skip)
   int start, len, tile_base, bcoord, qb, h, n, last_kb;
-  int j0;       // first list entry of this item (a chunk of a split row; 0 otherwise)
-  int entry;    // chunk entry (partial-result slot) or -1 for a whole row
-  int nchunks;  // chunks of the split row
-  int srow;     // split-row index (completion counter)
-  int pad[3];
+  int j0;     // first list entry of this item (a chunk of a split row; 0 otherwise)
+  int chunk;  // split_code(entry, chunk, nchunks) of a chunk of a split row, or -1 for a whole row
+  int pad[5];
 };
+
+// A chunk of a split row stores its unnormalised O (this thread's row, 64 columns from TMEM
+// address t_o) as fp32 to dst.  Out of line for the same reason as split_merge_row.
+__device__ __noinline__ void split_store_partial(uint32_t t_o, float* dst) {
+  float4* po = reinterpret_cast<float4*>(dst);
+#pragma unroll 1
+  for (int h = 0; h < 2; ++h) {
+    uint32_t o[32];
+    tmem_ld32(t_o + h * 32, o);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      po[h * 8 + i] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
+                                  __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]));
+  }
+}
+
+// The last chunk of a split row to finish merges the partial results of all its chunks (row
+// r, columns hh*64..+64 of this thread):  O = sum_c O_c 2^(m_c - M) / sum_c l_c 2^(m_c - M).
+// Kept out of line so the kernel's register allocation is not shaped by it.
+template <typename T>
+__device__ __noinline__ void split_merge_row(const float* p0, int nchunks, int r, int hh, int vr, T* orow,
+                                             int64_t o_ss) {
+  float M = -INFINITY;
+  for (int cix = 0; cix < nchunks; ++cix)
+    M = fmaxf(M, __ldcg(p0 + (int64_t)cix * (kSplitPartBytes / 4) + 128 * 128 + r));
+  float Lsum = 0.f;
+  for (int cix = 0; cix < nchunks; ++cix) {
+    const float* pc = p0 + (int64_t)cix * (kSplitPartBytes / 4) + 128 * 128;
+    Lsum += (__ldcg(pc + 128 + r) + __ldcg(pc + 256 + r)) * ex2_approx(__ldcg(pc + r) - M);
+  }
+  const float invL = 1.f / Lsum;
+  // 16 columns at a time, so the merge holds few registers
+#pragma unroll 1
+  for (int g = 0; g < 4; ++g) {
+    float acc[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+    for (int cix = 0; cix < nchunks; ++cix) {
+      const float* pc = p0 + (int64_t)cix * (kSplitPartBytes / 4);
+      const float sc = ex2_approx(__ldcg(pc + 128 * 128 + r) - M);
+      const float4* src = reinterpret_cast<const float4*>(pc + r * 128 + hh * 64 + g * 16);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 v4 = __ldcg(src + i);
+        acc[4 * i] += v4.x * sc;
+        acc[4 * i + 1] += v4.y * sc;
+        acc[4 * i + 2] += v4.z * sc;
+        acc[4 * i + 3] += v4.w * sc;
+      }
+    }
+    if (r < vr) {
+      uint4* dst = reinterpret_cast<uint4*>(orow + (int64_t)r * o_ss + hh * 64 + g * 16);
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          pk[i] = DT<T>::pack(acc[q * 8 + 2 * i] * invL, acc[q * 8 + 2 * i + 1] * invL);
+        dst[q] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+    }
+  }
+}
+
+// Epilogue of one chunk of a split row, for the 256 epilogue threads of a pipeline (row r,
+// half hh): stores the unnormalised O, the running max m and the row sum l of this chunk;
+// the chunk that finishes its row last merges all of them into the output.  Arrives on
+// o_empty once O is read, and passes the pipeline's group barrier (epi) twice, at phases ep
+// and ep + 1.  Returns false if a barrier wait gave up.  Kept out of line: inlined, its
+// code raised the kernel's register pressure and slowed the softmax loop.
+template <typename T>
+__device__ __noinline__ bool split_chunk_epilogue(uint32_t t_o, int code, float m_use, float l, int r, int hh,
+                                                  int vr, T* orow, int64_t o_ss, float* sp_part, int* sp_counters,
+                                                  int* last_chunk, uint64_t* epi, uint64_t* o_empty, uint32_t ep,
+                                                  volatile int* abort) {
+  const int entry = code & (kSplitMaxEntries - 1), nchunks = code >> 24;
+  const int e0 = entry - ((code >> 17) & 127);  // the row's first entry
+  float* part = sp_part + (int64_t)entry * (kSplitPartBytes / 4);
+  split_store_partial(t_o, part + r * 128 + hh * 64);
+  tc_fence_before();
+  mbar_arrive(o_empty);  // O may be overwritten by the next item's first PV
+  if (hh == 0) part[128 * 128 + r] = m_use;
+  part[128 * 128 + 128 + hh * 128 + r] = l;
+  __threadfence();
+  mbar_arrive(epi);
+  if (!mbar_wait_warp_sleep(epi, ep & 1, abort)) return false;
+  if (hh == 0 && r == 0) *last_chunk = atomicAdd(sp_counters + e0, 1) == nchunks - 1;
+  mbar_arrive(epi);
+  if (!mbar_wait_warp_sleep(epi, (ep + 1) & 1, abort)) return false;
+  if (*(volatile int*)last_chunk) {
+    __threadfence();
+    split_merge_row<T>(sp_part + (int64_t)e0 * (kSplitPartBytes / 4), nchunks, r, hh, vr, orow, o_ss);
+  }
+  return true;
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -206,7 +300,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint64_t stream_once = l2_policy_evict_first();
     uint32_t it = 0, kseq = 0, vseq = 0, qld = 0, sfc = 0;
     // chunks of split rows come first in the work order (they are the longest work)
-    const int n_ent = A.split ? *A.sp_head : 0;
+    const int n_ent = A.split ? A.sp_head[0] : 0;
+    const int split_thr = A.split ? A.sp_head[3] : 0x7fffffff;  // only rows above it can be split
     bool ok = true;
     while (ok) {
       const int slot = it & 1;
@@ -233,16 +328,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           f.h = h;
           const int64_t row = (int64_t)f.h * A.P.tiles_ub + s.tile_base + qb;
           const int n_row = max(0, min(__ldg(A.cnt + row), qb + 1));
-          f.entry = -1;
+          f.chunk = -1;
           if (id < n_ent) {  // one chunk of a split row
             f.j0 = se.chunk * kSplitChunk;
             f.n = min(kSplitChunk, n_row - f.j0);
-            f.entry = id;
-            f.nchunks = se.nchunks;
-            f.srow = se.srow;
+            f.chunk = split_code(id, se.chunk, se.nchunks);
           } else {
             f.n = n_row;
-            if (A.split && __ldg(A.sp_rowidx + row) >= 0) f.valid = 2;  // done as chunks
+            if (n_row > split_thr && __ldg(A.sp_rowidx + row) >= 0) f.valid = 2;  // done as chunks
           }
           lst = A.idx + row * A.P.cap + f.j0;
           f.last_kb = f.n > 0 ? __ldg(lst + f.n - 1) : -1;
@@ -605,6 +698,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       ++oc;
       tc_fence_after();
       const unsigned long long te0 = clk();
+      if (f.chunk >= 0) {  // a chunk of a split row
+        const bool ok2 = split_chunk_epilogue<T>(t_o, f.chunk, m_use, l, r, hh, vr, orow, A.o_ss, A.sp_part,
+                                                 A.sp_counters, last_chunk, epi + x, o_empty + x, ep, abort);
+        ep += 2;
+        if (!ok2) break;
+        if (hh * 128 + r == 0) mbar_arrive(stage_free + x);  // the V tile was not used for staging
+        pa.add(11, clk() - te0);
+        continue;
+      }
       uint32_t oa[32], ob[32];
       tmem_ld32(t_o, oa);
       tmem_ld32(t_o + 32, ob);
@@ -612,67 +714,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(o_empty + x);  // O_x may be overwritten by the next item's first PV
-      if (f.entry >= 0) {
-        // a chunk of a split row: store its unnormalised O, m and l; the last chunk of the
-        // row to finish merges all of them into the output
-        const int et = hh * 128 + r;
-        float* part = A.sp_part + (int64_t)f.entry * (kSplitPartBytes / 4);
-        float4* po = reinterpret_cast<float4*>(part + r * 128 + hh * 64);
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          po[i] = make_float4(__uint_as_float(oa[4 * i]), __uint_as_float(oa[4 * i + 1]), __uint_as_float(oa[4 * i + 2]),
-                              __uint_as_float(oa[4 * i + 3]));
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          po[8 + i] = make_float4(__uint_as_float(ob[4 * i]), __uint_as_float(ob[4 * i + 1]),
-                                  __uint_as_float(ob[4 * i + 2]), __uint_as_float(ob[4 * i + 3]));
-        if (hh == 0) part[128 * 128 + r] = m_use;
-        part[128 * 128 + 128 + hh * 128 + r] = l;
-        __threadfence();
-        if (!group_sync()) break;
-        if (et == 0) *last_chunk = atomicAdd(A.sp_counters + f.srow, 1) == f.nchunks - 1;
-        if (!group_sync()) break;
-        if (*(volatile int*)last_chunk) {
-          __threadfence();
-          const float* p0 = A.sp_part + (int64_t)(f.entry - f.j0 / kSplitChunk) * (kSplitPartBytes / 4);
-          float M = -INFINITY;
-          for (int cix = 0; cix < f.nchunks; ++cix)
-            M = fmaxf(M, __ldcg(p0 + (int64_t)cix * (kSplitPartBytes / 4) + 128 * 128 + r));
-          float acc[64];
-#pragma unroll
-          for (int i = 0; i < 64; ++i) acc[i] = 0.f;
-          float Lsum = 0.f;
-          for (int cix = 0; cix < f.nchunks; ++cix) {
-            const float* pc = p0 + (int64_t)cix * (kSplitPartBytes / 4);
-            const float sc = ex2_approx(__ldcg(pc + 128 * 128 + r) - M);
-            Lsum += (__ldcg(pc + 128 * 128 + 128 + r) + __ldcg(pc + 128 * 128 + 256 + r)) * sc;
-            const float4* src = reinterpret_cast<const float4*>(pc + r * 128 + hh * 64);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float4 v4 = __ldcg(src + i);
-              acc[4 * i] += v4.x * sc;
-              acc[4 * i + 1] += v4.y * sc;
-              acc[4 * i + 2] += v4.z * sc;
-              acc[4 * i + 3] += v4.w * sc;
-            }
-          }
-          const float invL = 1.f / Lsum;
-          if (r < vr) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + (int64_t)r * A.o_ss + hh * 64);
-#pragma unroll
-            for (int q4 = 0; q4 < 8; ++q4) {
-              uint32_t pk[4];
-#pragma unroll
-              for (int i = 0; i < 4; ++i)
-                pk[i] = DT<T>::pack(acc[q4 * 8 + 2 * i] * invL, acc[q4 * 8 + 2 * i + 1] * invL);
-              dst[q4] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            }
-          }
-        }
-        if (et == 0) mbar_arrive(stage_free + x);  // the V tile was not used for staging
-        pa.add(11, clk() - te0);
-        continue;
-      }
       if (!group_sync()) break;
       const float inv = 1.f / (l + xl[(hh ^ 1) * 128 + r]);
       uint8_t* stage = smem + x * 3 * kAttnTile + 2 * kAttnTile;  // V tile: its last PV has completed
