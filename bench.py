@@ -168,6 +168,24 @@ def algorithmic(w, hq, hk, E):
 
 
 # --------------------------------------------------------------------------- CPU arm
+def split_plan_runs_dense(seqlen, hq, cap, sms, sink=2, window=4, last_n=2):
+    """Whether fpb_prefill_dense runs the long-row split plan: it skips it when even a
+    full-length row is within the split threshold (1.2x the listed blocks per attention
+    pipeline) for the fewest blocks the search can list (its structural blocks)."""
+    nb = -(-seqlen // 128)
+    if cap <= 64:
+        return False
+    lb = 0
+    for qb in range(nb):
+        if qb >= nb - last_n:
+            lb += qb + 1
+        else:
+            s_end, w_lo = min(sink, qb + 1), max(0, qb - window + 1)
+            lb += s_end + (qb + 1 - w_lo) - max(0, s_end - w_lo)
+    grid = min(sms, nb * hq)
+    return not (min(cap, nb) * 5 * 2 * grid <= lb * hq * 6)
+
+
 def cpu_sample(w, seconds_budget=20.0):
     """Time the CPU restatement on a bounded sample of the layer and extrapolate.
 
@@ -265,6 +283,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-gather", action="store_true",
+                    help="N>1: skip the separately timed all-gather of the head shards into the full output")
     ap.add_argument("--shard", default=None, help="R/N: run rank R's share of an N-GPU job alone on one GPU "
                     "(no process group; for studying the per-rank work)")
     a = ap.parse_args()
@@ -299,7 +319,10 @@ def main():
     from flashprefill_b200 import _ops
 
     if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"))
+        import datetime
+        # a collective that one rank never joins fails in two minutes instead of NCCL's ten
+        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"),
+                                timeout=datetime.timedelta(seconds=120))
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
     from flashprefill_b200.sharding import head_shard
@@ -333,7 +356,14 @@ def main():
         else:
             _ops.attention_dense(q[None], k[None], v[None], out[None], ws)
 
+    def api_step():  # the call a user makes (flash_prefill / flash_prefill_varlen_func)
+        if w.varlen:
+            _ops.prefill_varlen(q, k, v, out, cu, maxlen, w.alpha, 128, 2, 4, 2, workspace=ws)
+        else:
+            _ops.prefill_dense(q[None], k[None], v[None], out[None], 128, 2, 4, w.alpha, 2, 0, workspace=ws)
+
     for _ in range(max(3, a.warmup)):
+        api_step()
         step()
     torch.cuda.synchronize()
     fp.check_device_error(ws)
@@ -342,25 +372,33 @@ def main():
     real_tiles = sum(math.ceil(x / 128) for x in w.seqlens)
     E_local = int(cnt[:, :real_tiles].sum().item())
 
-    # ---- timed region (device-resident inputs)
-    evs = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(a.steps)]
+    # ---- timed region (device-resident inputs): the public entry point, one call per step
+    evh = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(2)) for _ in range(a.steps)]
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         t_wall = time.perf_counter()
-        for e0, e1, e2 in evs:
+        for e0, e2 in evh:
             e0.record(stream)
-            step(e1)
+            api_step()
             e2.record(stream)
         torch.cuda.synchronize()
         t_wall = time.perf_counter() - t_wall
     if world > 1:
         dist.barrier()
     clocks = clk.summary()
+    t_step = sum(e0.elapsed_time(e2) for e0, e2 in evh) / a.steps
+    # ---- breakdown (not the headline): search and attention entry points, an event between
+    evs = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(a.steps)]
+    torch.cuda.synchronize()
+    for e0, e1, e2 in evs:
+        e0.record(stream)
+        step(e1)
+        e2.record(stream)
+    torch.cuda.synchronize()
     t_search = sum(e0.elapsed_time(e1) for e0, e1, e2 in evs) / a.steps
     t_attn = sum(e1.elapsed_time(e2) for e0, e1, e2 in evs) / a.steps
-    t_step = sum(e0.elapsed_time(e2) for e0, e1, e2 in evs) / a.steps
     stats = torch.tensor([t_step, t_search, t_attn, E_local], dtype=torch.float64, device=dev)
     mx, tot = stats.clone(), stats.clone()
     if world > 1:
@@ -432,6 +470,38 @@ def main():
                "d2h_bytes_per_step": int(out.numel() * out.element_size() * world), "steps": n_e2e,
                "pipelined": "upload / compute / download on three streams, device buffers double-buffered"}
 
+    # ---- optional output gather (N>1), timed on its own: every rank receives the other ranks'
+    # head shards over NVLink (NCCL all-gather into a rank-major buffer) and reorders them into
+    # the full (T, Hq, D) output.  The headline value excludes it; a caller whose next
+    # operator is row-parallel over heads (o_proj under tensor parallelism) never needs it.
+    gather = None
+    if world > 1 and not a.no_gather:
+        stage = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=dev)
+        full = torch.empty((T, world * hq_l, w.d), dtype=out.dtype, device=dev)
+
+        def gstep():
+            dist.all_gather_into_tensor(stage, out)
+            full.view(T, world, hq_l, w.d).copy_(stage.permute(1, 0, 2, 3))
+
+        for _ in range(3):
+            gstep()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize()
+        g0.record(stream)
+        for _ in range(a.steps):
+            gstep()
+        g1.record(stream)
+        torch.cuda.synchronize()
+        g_ms = torch.tensor([g0.elapsed_time(g1) / a.steps], dtype=torch.float64, device=dev)
+        dist.all_reduce(g_ms, op=dist.ReduceOp.MAX)
+        g_ms = float(g_ms)
+        ok = bool(torch.equal(full[:, rank * hq_l:(rank + 1) * hq_l], out))
+        recv = (world - 1) * out.numel() * out.element_size()
+        gather = {"ms": round(g_ms, 4), "ms_per_layer_with_gather": round(ms + g_ms, 4),
+                  "nvlink_bytes_in_per_rank": recv, "gbs_in_per_rank": round(recv / (g_ms * 1e-3) / 1e9, 1),
+                  "own_shard_in_place": ok,
+                  "how": "NCCL all_gather_into_tensor + reorder copy to (T, Hq, D), max over ranks"}
     # ---- CPU baseline (rank 0, N=1 only)
     cpu = None
     exact = None
@@ -460,6 +530,13 @@ def main():
               "algorithmic": "2*(S*Hq*D + S*Hk*D) + 4*E + 4*Hq*NB bytes", "peak_kind": f"{peak_kind} HBM copy"}
     nbs = [math.ceil(L_ / 128) for L_ in w.seqlens]
     P_pairs = w.hq * sum(nb * (nb + 1) // 2 for nb in nbs)
+    # kernels one public call launches: pooled keys, search, attention; varlen adds its prep
+    # kernel; the long-row split plan adds two unless the dense entry rules it out on the host
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    plan = L["cap"] > 64 and not os.environ.get("FLASHPREFILL_B200_NO_SPLIT")
+    if plan and not w.varlen:
+        plan = split_plan_runs_dense(T, hq_l, L["cap"], sms)
+    launches = 3 + (1 if w.varlen else 0) + (2 if plan else 0)
     line = {"metric": METRIC, "value": round(ms, 4), "unit": UNIT, "n_gpus": world, "steps": a.steps,
             "warmup": max(3, a.warmup), "ms_per_step": round(ms, 4), "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
@@ -471,7 +548,7 @@ def main():
             "executed_pairs": E_total, "density": round(E_total / P_pairs, 5),
             "roofline": roof, "roofline_search": roof_s, "e2e": e2e, "cpu_baseline": cpu,
             "mask_exactness": exact,
-            "gpu_launches": a.steps * (3 + (1 if w.varlen else 0)),
+            "gpu_launches": a.steps * launches, "output_gather": gather,
             "clocks": clocks, "wall_s_timed": round(t_wall, 3)}
     print(json.dumps(line))
     if world > 1:
