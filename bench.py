@@ -40,6 +40,16 @@ sys.path.insert(0, ROOT)
 
 METRIC = "sparse-prefill attn ms/layer @128K on 1/8 B200; TC util; mask exactness"
 UNIT = "ms/layer"
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of
+# each kernel on the full single-GPU workload (1 pass; the commands and figures are in
+# profiles/dram_traffic.md).  Reported as roofline traffic for those workloads on one GPU
+# with all heads; other runs (shards, N > 1, other workloads) report null.
+NCU_TRAFFIC = {
+    "llama3_8b_layer_128k": {"sparse_attn_kernel": 2235387136 + 1032059392,
+                             "block_search_persistent_kernel": 1074923264 + 5547008},
+    "cfg1_llama3_8b_32k": {"sparse_attn_kernel": 503862272 + 227547904,
+                           "block_search_persistent_kernel": 267095552 + 3992320},
+}
 
 
 def load_peaks():
@@ -516,17 +526,21 @@ def main():
             dist.destroy_process_group()
         return
     hbm, tflops, _, peak_kind = load_peaks()
+    whole = world == 1 and not shard and not os.environ.get("FLASHPREFILL_B200_NO_SPLIT")
+    traffic = NCU_TRAFFIC.get(w.name, {}) if whole else {}
     sb, af, sf = algorithmic(w, hq_l, hk_l, E_local)
     t_a, t_s = float(mx[2]), float(mx[1])
     ach = af / (t_a * 1e-3) / 1e12
     roof = {"bound": "tensor", "achieved": round(ach, 2), "peak": tflops, "unit": "TFLOP/s",
-            "frac": round(ach / tflops, 4), "traffic": None, "kernel": "sparse_attn_kernel", "ms": round(t_a, 4),
+            "frac": round(ach / tflops, 4), "traffic": traffic.get("sparse_attn_kernel"),
+            "kernel": "sparse_attn_kernel", "ms": round(t_a, 4),
             "algorithmic": f"E*4*128*128*128 FLOP, E={E_local} executed block pairs on this rank",
             "peak_kind": f"{peak_kind} burst bf16 (of measured)" if peak_kind == "measured" else "fallback"}
     sach = sb / (t_s * 1e-3) / 1e9
     roof_s = {"bound": "hbm", "achieved": round(sach, 1), "peak": hbm, "unit": "GB/s", "frac": round(sach / hbm, 4),
               "ms": round(t_s, 4), "mma_tflops": round(sf / (t_s * 1e-3) / 1e12, 1),
               "kernels": "block_mean_kernel + block_search_kernel",
+              "traffic_search_kernel": traffic.get("block_search_persistent_kernel"),
               "algorithmic": "2*(S*Hq*D + S*Hk*D) + 4*E + 4*Hq*NB bytes", "peak_kind": f"{peak_kind} HBM copy"}
     nbs = [math.ceil(L_ / 128) for L_ in w.seqlens]
     P_pairs = w.hq * sum(nb * (nb + 1) // 2 for nb in nbs)
