@@ -294,7 +294,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-gather", action="store_true",
-                    help="N>1: skip the separately timed all-gather of the head shards into the full output")
+                    help="N>1: skip the separately timed gathers of the head shards into the full output")
     ap.add_argument("--shard", default=None, help="R/N: run rank R's share of an N-GPU job alone on one GPU "
                     "(no process group; for studying the per-rank work)")
     a = ap.parse_args()
@@ -480,38 +480,69 @@ def main():
                "d2h_bytes_per_step": int(out.numel() * out.element_size() * world), "steps": n_e2e,
                "pipelined": "upload / compute / download on three streams, device buffers double-buffered"}
 
-    # ---- optional output gather (N>1), timed on its own: every rank receives the other ranks'
-    # head shards over NVLink (NCCL all-gather into a rank-major buffer) and reorders them into
-    # the full (T, Hq, D) output.  The headline value excludes it; a caller whose next
-    # operator is row-parallel over heads (o_proj under tensor parallelism) never needs it.
+    # ---- optional output gather (N>1), timed on its own.  The headline value excludes it; a
+    # caller whose next operator is row-parallel over heads (o_proj under tensor parallelism)
+    # never needs it.  Two ways, both leaving the full (T, Hq, D) output on every rank:
+    #   nccl:  the layer as above, then an NCCL all-gather of the head shards into a rank-major
+    #          buffer and one reorder copy;
+    #   fused: the attention epilogue writes every output tile into all ranks' full outputs
+    #          over NVLink (fpb_prefill_dense_peers, peers mapped by CUDA IPC), then a
+    #          one-element all-reduce orders the ranks (a stream-ordered cross-GPU barrier).
     gather = None
     if world > 1 and not a.no_gather:
         stage = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=dev)
         full = torch.empty((T, world * hq_l, w.d), dtype=out.dtype, device=dev)
 
-        def gstep():
+        def nccl_step():
+            api_step()
             dist.all_gather_into_tensor(stage, out)
             full.view(T, world, hq_l, w.d).copy_(stage.permute(1, 0, 2, 3))
 
-        for _ in range(3):
-            gstep()
-        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        dist.barrier()
-        torch.cuda.synchronize()
-        g0.record(stream)
-        for _ in range(a.steps):
-            gstep()
-        g1.record(stream)
-        torch.cuda.synchronize()
-        g_ms = torch.tensor([g0.elapsed_time(g1) / a.steps], dtype=torch.float64, device=dev)
-        dist.all_reduce(g_ms, op=dist.ReduceOp.MAX)
-        g_ms = float(g_ms)
-        ok = bool(torch.equal(full[:, rank * hq_l:(rank + 1) * hq_l], out))
+        def timed(fn):
+            for _ in range(3):
+                fn()
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            dist.barrier()
+            torch.cuda.synchronize()
+            g0.record(stream)
+            for _ in range(a.steps):
+                fn()
+            g1.record(stream)
+            torch.cuda.synchronize()
+            t = torch.tensor([g0.elapsed_time(g1) / a.steps], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t)
+
         recv = (world - 1) * out.numel() * out.element_size()
-        gather = {"ms": round(g_ms, 4), "ms_per_layer_with_gather": round(ms + g_ms, 4),
-                  "nvlink_bytes_in_per_rank": recv, "gbs_in_per_rank": round(recv / (g_ms * 1e-3) / 1e9, 1),
-                  "own_shard_in_place": ok,
-                  "how": "NCCL all_gather_into_tensor + reorder copy to (T, Hq, D), max over ranks"}
+        t_nccl = timed(nccl_step)
+        gather = {"nvlink_bytes_in_per_rank": recv,
+                  "nccl": {"ms_per_layer_with_gather": round(t_nccl, 4), "gather_ms": round(t_nccl - ms, 4),
+                           "how": "layer, then NCCL all_gather_into_tensor + reorder copy to (T, Hq, D)"}}
+        if not w.varlen:
+            from flashprefill_b200.peer_output import PeerOutputs
+            full2 = torch.full((T, world * hq_l, w.d), float("nan"), dtype=out.dtype, device=dev)
+            mine = full2[:, hq0:hq1]
+            peers = PeerOutputs(full2)
+            pptr = peers.peer_ptrs((mine.data_ptr() - full2.data_ptr()))
+            flag = torch.zeros(1, dtype=torch.float32, device=dev)
+
+            def fused_step():
+                _ops.prefill_dense(q[None], k[None], v[None], mine[None], 128, 2, 4, w.alpha, 2, 0,
+                                   workspace=ws, out_peers=pptr)
+                dist.all_reduce(flag)
+
+            t_fused = timed(fused_step)
+            torch.cuda.synchronize()
+            dist.barrier()
+            same = torch.tensor([1.0 if torch.equal(full2, full) else 0.0], device=dev)
+            dist.all_reduce(same, op=dist.ReduceOp.MIN)
+            peers.close()
+            gather["fused"] = {"ms_per_layer_with_gather": round(t_fused, 4),
+                               "gather_ms": round(t_fused - ms, 4),
+                               "equals_nccl_gather_on_all_ranks": bool(same.item() == 1.0),
+                               "how": "attention epilogue stores every tile to all ranks' full outputs "
+                                      "(16-byte peer stores over NVLink, CUDA IPC mappings), then a "
+                                      "1-element all-reduce as barrier"}
     # ---- CPU baseline (rank 0, N=1 only)
     cpu = None
     exact = None

@@ -133,19 +133,28 @@ def _dense_args(q, k, v, out):
 
 
 def prefill_dense(q, k, v, out, block_size, attention_sink, window_size, alpha, last_n_block_full, min_budget,
-                  workspace: torch.Tensor | None = None):
-    """Full operator on (B,S,H,D) tensors; writes ``out`` in place.  Returns the workspace."""
+                  workspace: torch.Tensor | None = None, out_peers=None):
+    """Full operator on (B,S,H,D) tensors; writes ``out`` in place.  Returns the workspace.
+
+    ``out_peers``: device addresses (ints) of the same output slice in other GPUs' copies of
+    the output; every output tile is written there too (fpb_prefill_dense_peers)."""
     lib = _lib.load()
     q, k, v, B, S, Hq, Hk, D = _dense_args(q, k, v, out)
     code = _dtype_code(q)
     tgt = out if _tma_ok(out) else torch.empty_like(q)
+    if out_peers and tgt is not out:
+        raise ValueError("out must be a TMA-compatible strided view when out_peers is given")
     ws = workspace if workspace is not None else _workspace(lib.fpb_dense_workspace_bytes(B, S, Hq, Hk, D), q.device)
     stream = torch.cuda.current_stream(q.device).cuda_stream
     with torch.cuda.device(q.device):
-        rc = lib.fpb_prefill_dense(_P(q), _P(k), _P(v), _P(tgt), code, B, S, Hq, Hk, D, _strides(q, 3),
-                                   _strides(k, 3), _strides(v, 3), _strides(tgt, 3), int(block_size),
-                                   int(attention_sink), int(window_size), float(alpha), int(last_n_block_full),
-                                   int(min_budget), _MEAN_WARPS, _P(ws), ws.numel(), _P(stream))
+        args = (_P(q), _P(k), _P(v), _P(tgt), code, B, S, Hq, Hk, D, _strides(q, 3), _strides(k, 3), _strides(v, 3),
+                _strides(tgt, 3), int(block_size), int(attention_sink), int(window_size), float(alpha),
+                int(last_n_block_full), int(min_budget), _MEAN_WARPS, _P(ws), ws.numel())
+        if out_peers:
+            peers = (ctypes.c_void_p * len(out_peers))(*[int(p) for p in out_peers])
+            rc = lib.fpb_prefill_dense_peers(*args, peers, len(out_peers), _P(stream))
+        else:
+            rc = lib.fpb_prefill_dense(*args, _P(stream))
     _lib.check(rc)
     if tgt is not out:
         out.copy_(tgt)

@@ -337,7 +337,8 @@ int run_search(const Geometry& g, const void* q, const void* k, const int64_t qs
 
 int run_attention(const Geometry& g, const void* q, const void* k, const void* v, void* o, const int64_t qs[3],
                   const int64_t ks[3], const int64_t vs[3], const int64_t os[3], uint8_t* ws, const Layout& L,
-                  size_t ws_bytes, cudaStream_t stream, int64_t listed_lower_bound = 0) {
+                  size_t ws_bytes, cudaStream_t stream, int64_t listed_lower_bound = 0,
+                  void* const* out_peers = nullptr, int n_peers = 0) {
   SeqProblem P = make_problem(g, L, ws);
   const int rows = g.varlen ? g.total_tokens : g.seqlen;
   const int batch = g.varlen ? 1 : g.batch;
@@ -401,22 +402,23 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
     static const unsigned long long zeros[kProfSlots] = {};
     FPB_CUDA(cudaMemcpyToSymbolAsync(g_attn_prof, zeros, sizeof(zeros), 0, cudaMemcpyHostToDevice, stream));
   }
+  A.n_peers = n_peers;
+  for (int i = 0; i < n_peers; ++i) A.peer_out[i] = out_peers[i];
+  // the peer-writing instance only when there are peers: the plain one is the hot path
+  using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, AttnArgs);
+  const KernelFn kern =
+      g.dtype == FPB_BF16 ? (n_peers ? sparse_attn_kernel<__nv_bfloat16, true> : sparse_attn_kernel<__nv_bfloat16, false>)
+                          : (n_peers ? sparse_attn_kernel<__half, true> : sparse_attn_kernel<__half, false>);
   {
     cudaFuncAttributes fa{};
-    FPB_CUDA(cudaFuncGetAttributes(&fa, g.dtype == FPB_BF16 ? (const void*)sparse_attn_kernel<__nv_bfloat16>
-                                                             : (const void*)sparse_attn_kernel<__half>));
+    FPB_CUDA(cudaFuncGetAttributes(&fa, (const void*)kern));
     if (fa.numRegs != kAttnLaunchRegs)
       return fail(FPB_ECUDA, "attention kernel compiled with %d registers/thread, %d expected by its register split",
                   fa.numRegs, kAttnLaunchRegs);
   }
   const size_t smem = attn_smem_bytes();
-  if (g.dtype == FPB_BF16) {
-    FPB_TRY(set_smem(sparse_attn_kernel<__nv_bfloat16>, smem));
-    sparse_attn_kernel<__nv_bfloat16><<<grid, kAttnThreads, smem, stream>>>(tm_q, tm_k, tm_v, tm_o, A);
-  } else {
-    FPB_TRY(set_smem(sparse_attn_kernel<__half>, smem));
-    sparse_attn_kernel<__half><<<grid, kAttnThreads, smem, stream>>>(tm_q, tm_k, tm_v, tm_o, A);
-  }
+  FPB_TRY(set_smem(kern, smem));
+  kern<<<grid, kAttnThreads, smem, stream>>>(tm_q, tm_k, tm_v, tm_o, A);
   FPB_CUDA(cudaGetLastError());
   if (A.trace) {  // debug: CTA 0's event trace, written to the file the variable names
     unsigned int n = 0;
@@ -635,6 +637,31 @@ int fpb_prefill_dense(const void* q, const void* k, const void* v, void* out, in
                      mean_model, ws, L, st));
   return run_attention(g, q, k, v, out, q_strides, k_strides, v_strides, o_strides, ws, L, workspace_bytes, st,
                        dense_listed_lower_bound(batch, seqlen, hq, attention_sink, window_size, last_n_block_full));
+}
+
+int fpb_prefill_dense_peers(const void* q, const void* k, const void* v, void* out, int dtype, int batch, int seqlen,
+                            int hq, int hk, int head_dim, const int64_t* q_strides, const int64_t* k_strides,
+                            const int64_t* v_strides, const int64_t* o_strides, int block_size, int attention_sink,
+                            int window_size, float alpha, int last_n_block_full, int min_budget, int mean_model,
+                            void* workspace, size_t workspace_bytes, void* const* out_peers, int n_peers,
+                            void* stream) {
+  FPB_CHECK_ARG(n_peers >= 0 && n_peers <= kMaxOutPeers, "n_peers (%d) must be in [0, %d]", n_peers, kMaxOutPeers);
+  FPB_CHECK_ARG(n_peers == 0 || out_peers != nullptr, "out_peers is NULL");
+  for (int i = 0; i < n_peers; ++i)
+    FPB_CHECK_ARG(out_peers[i] != nullptr && reinterpret_cast<uintptr_t>(out_peers[i]) % 16 == 0,
+                  "out_peers[%d] must be a 16-byte aligned device pointer", i);
+  FPB_TRY(check_dense(q, k, dtype, batch, seqlen, hq, hk, head_dim, q_strides, k_strides, block_size));
+  FPB_TRY(check_dense_vo(v, out, v_strides, o_strides));
+  const Layout L = make_layout(0, batch, seqlen, 0, hq, hk);
+  FPB_TRY(check_ws(workspace, workspace_bytes, L));
+  Geometry g{0, batch, seqlen, 0, 0, batch, hq, hk, dtype, nullptr};
+  auto* ws = static_cast<uint8_t*>(workspace);
+  auto st = static_cast<cudaStream_t>(stream);
+  FPB_TRY(run_search(g, q, k, q_strides, k_strides, attention_sink, window_size, alpha, last_n_block_full, min_budget,
+                     mean_model, ws, L, st));
+  return run_attention(g, q, k, v, out, q_strides, k_strides, v_strides, o_strides, ws, L, workspace_bytes, st,
+                       dense_listed_lower_bound(batch, seqlen, hq, attention_sink, window_size, last_n_block_full),
+                       out_peers, n_peers);
 }
 
 int fpb_prefill_varlen(const void* q, const void* k, const void* v, void* o, int dtype, const int32_t* cu_seqlens,

@@ -29,6 +29,8 @@
 
 namespace fpb {
 
+constexpr int kMaxOutPeers = 7;  // peers of an output gather (8 GPUs of one NVSwitch domain)
+
 struct AttnArgs {
   SeqProblem P;
   float c;                   // fp32(1/sqrt(D)) * fp32(log2 e)
@@ -48,6 +50,10 @@ struct AttnArgs {
   const int* sp_rowidx;      // [hq][tiles_ub] split-row index or -1 (rows over the threshold)
   int* sp_counters;          // chunks finished per split row, at the row's first entry
   float* sp_part;            // per chunk entry: O [128][128], m [128], l [2][128]
+  // other GPUs' copies of the output (same layout and strides as `out`, reached over
+  // NVLink): the epilogue writes every output tile there too (kernel instance kPeers)
+  int n_peers;
+  void* peer_out[kMaxOutPeers];
 };
 
 constexpr int kAttnThreads = 640;
@@ -211,7 +217,15 @@ __device__ __noinline__ bool split_chunk_epilogue(uint32_t t_o, int code, float 
   return true;
 }
 
-template <typename T>
+// Copy `bytes` (a multiple of 16) from src to the same byte offset of every peer output.
+__device__ __forceinline__ void copy_row_to_peers(const AttnArgs& A, int64_t byte_off, const void* src, int bytes) {
+  for (int p = 0; p < A.n_peers; ++p) {
+    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(A.peer_out[p]) + byte_off);
+    for (int i = 0; i < bytes / 16; ++i) dst[i] = reinterpret_cast<const uint4*>(src)[i];
+  }
+}
+
+template <typename T, bool kPeers>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     sparse_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -590,6 +604,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           uint4* dst = reinterpret_cast<uint4*>(orow + (int64_t)r * A.o_ss + hh * 64);
 #pragma unroll
           for (int i = 0; i < 8; ++i) dst[i] = make_uint4(0, 0, 0, 0);
+          if constexpr (kPeers)
+            copy_row_to_peers(A, reinterpret_cast<const uint8_t*>(dst) - reinterpret_cast<const uint8_t*>(A.out),
+                              dst, 128);
         }
         continue;
       }
@@ -703,6 +720,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                                                  A.sp_counters, last_chunk, epi + x, o_empty + x, ep, abort);
         ep += 2;
         if (!ok2) break;
+        if constexpr (kPeers) {
+          if (*(volatile int*)last_chunk && r < vr) {  // this chunk merged the row: send it on
+            const T* src = orow + (int64_t)r * A.o_ss + hh * 64;
+            copy_row_to_peers(A, reinterpret_cast<const uint8_t*>(src) - reinterpret_cast<const uint8_t*>(A.out),
+                              src, 128);
+          }
+        }
         if (hh * 128 + r == 0) mbar_arrive(stage_free + x);  // the V tile was not used for staging
         pa.add(11, clk() - te0);
         continue;
@@ -733,6 +757,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       fence_proxy_async_smem();
       if (!group_sync()) break;
       const int et = hh * 128 + r;
+      if constexpr (kPeers) {
+        // the staged tile to every peer's output, 16 bytes per store, rows r < vr
+        const int64_t row0 = reinterpret_cast<const uint8_t*>(orow) - reinterpret_cast<const uint8_t*>(A.out);
+        for (int p = 0; p < A.n_peers; ++p) {
+          uint8_t* pbase = reinterpret_cast<uint8_t*>(A.peer_out[p]) + row0;
+          for (int e = et; e < vr * 16; e += 256) {
+            const int rr = e >> 4, cidx = e & 15;
+            const uint4 v = *reinterpret_cast<const uint4*>(stage + (cidx >> 3) * kAttnHalf + rr * 128 +
+                                                           (((cidx & 7) ^ (rr & 7)) << 4));
+            *reinterpret_cast<uint4*>(pbase + ((int64_t)rr * A.o_ss + cidx * 8) * (int64_t)sizeof(T)) = v;
+          }
+        }
+        if (!group_sync()) break;
+      }
       if (vr == kBlock) {
         if (et == 0) {
           const int qrow = f.start + f.qb * kBlock;
@@ -757,6 +795,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // the epilogue waits only until its stores have read the staging tile; their global
     // writes must be complete before the thread exits
     tma_store_wait_all();
+    if constexpr (kPeers) __threadfence_system();  // peer stores ordered before what follows
   }
 
   if (threadIdx.x == 0) pa.add(18, clk() - t_kernel0);

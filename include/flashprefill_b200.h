@@ -100,6 +100,22 @@ FPB_API int fpb_prefill_varlen(const void* q, const void* k, const void* v, void
                                int attention_sink, int window_size, float alpha, int last_n_block, int mean_model,
                                void* workspace, size_t workspace_bytes, void* stream);
 
+/* fpb_prefill_dense for one rank of a head-sharded layer that also needs the full output on
+ * every GPU (the gather of head shards; the reference has no multi-GPU path of its own).
+ * `out` is this rank's head slice of its full (B, S, Hq, D) output; out_peers[i] is the
+ * address of the same slice in another GPU's copy of that output (identical layout and
+ * strides), reachable from this GPU (peer access or a symmetric-memory mapping).  The
+ * attention epilogue writes every output tile to `out` and, with 16-byte stores over
+ * NVLink, to each peer, so the gather overlaps the attention.  The call returns when the
+ * work is queued: the caller orders the peers' reads after every rank's kernel (a
+ * cross-GPU barrier on the stream).  n_peers <= 7. */
+FPB_API int fpb_prefill_dense_peers(const void* q, const void* k, const void* v, void* out, int dtype, int batch,
+                                    int seqlen, int hq, int hk, int head_dim, const int64_t* q_strides,
+                                    const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                                    int block_size, int attention_sink, int window_size, float alpha,
+                                    int last_n_block_full, int min_budget, int mean_model, void* workspace,
+                                    size_t workspace_bytes, void* const* out_peers, int n_peers, void* stream);
+
 /* Search stage only (pooled keys + block lists into the workspace): replaces
  * compute_mean_vector + compute_block_score + normalize_scores + deal_output_score
  * (ops/flashprefill_native_forward.py:22-188,347-403). */

@@ -209,3 +209,24 @@ def test_split_long_rows_match_oracle(lens, varlen, monkeypatch):
         err = np.abs(o.float().cpu().numpy() - ref)[sel]
         print(f"  split={split} rows={len(rows)} max-abs {err.max():.3e} mean-abs {err.mean():.3e}")
         assert err.max() <= gu.MAX_ABS and err.mean() <= gu.MEAN_ABS
+
+
+def test_prefill_peers_writes_every_copy():
+    """fpb_prefill_dense_peers: one rank of a head-sharded layer (heads 4-7 of 8) writes its
+    output slice into its own full output and into two 'peer' copies (other buffers on this
+    GPU stand in for other GPUs' memory).  Every copy of the slice equals the plain prefill
+    bit for bit, and the other heads are left alone.  20,000 tokens: split rows and a
+    partial last block go through the peer path too."""
+    S, hq, hk, HQ = 20000, 4, 1, 8
+    q, k, v, cu = gu.make_packed([S], hq, hk, torch.bfloat16, seed0=77)
+    qd, kd, vd = (t[None].to(DEV) for t in (q, k, v))
+    ref = torch.empty_like(qd)
+    fp.flash_prefill(qd, kd, vd, ref, 128, 2, 4, 0.05, 2, 0)
+    fulls = [torch.full((1, S, HQ, 128), 7.0, dtype=torch.bfloat16, device=DEV) for _ in range(3)]
+    slices = [f[:, :, 4:8] for f in fulls]
+    _ops.prefill_dense(qd, kd, vd, slices[0], 128, 2, 4, 0.05, 2, 0,
+                       out_peers=[slices[1].data_ptr(), slices[2].data_ptr()])
+    torch.cuda.synchronize()
+    for i, (f, sl) in enumerate(zip(fulls, slices)):
+        assert torch.equal(sl, ref), f"copy {i} differs from the plain prefill"
+        assert bool((f[:, :, :4] == 7.0).all()), f"copy {i}: heads outside the slice were written"
