@@ -93,6 +93,24 @@ def test_invalid_arguments_rejected_before_launch(lib, over, msg):
     assert msg in lib.fpb_last_error().decode()
 
 
+@pytest.mark.parametrize("peers,n,msg", [
+    ([4096], 8, "n_peers"),
+    (None, 1, "out_peers is NULL"),
+    ([0], 1, "out_peers[0]"),
+    ([4096, 4104], 2, "out_peers[1]"),
+])
+def test_peer_entry_rejects_bad_peers(lib, peers, n, msg):
+    """fpb_prefill_dense_peers checks its peer list on the host before anything runs."""
+    st = _lib.i64arr([1024 * 4 * 128, 4 * 128, 128])
+    sk = _lib.i64arr([1024 * 2 * 128, 2 * 128, 128])
+    P = ctypes.c_void_p
+    arr = (P * len(peers))(*peers) if peers is not None else None
+    rc = lib.fpb_prefill_dense_peers(P(256), P(512), P(768), P(1024), 0, 1, 1024, 4, 2, 128, st, sk, sk, st, 128,
+                                     2, 4, 0.1, 2, 0, 4, P(4096), 1 << 30, arr, n, None)
+    assert rc == _lib.FPB_EINVAL
+    assert msg in lib.fpb_last_error().decode()
+
+
 def test_python_rejects_cpu_tensors():
     import torch
     import flashprefill_b200 as fp
