@@ -461,7 +461,9 @@ def main():
 
         for i in range(2):
             e2e_step(i)
-        n_e2e = max(2, min(a.steps, 5))
+        # all --steps steps: the timed region ends with the last step's compute and download
+        # (the pipeline's drain), which the whole-job figure includes
+        n_e2e = max(2, a.steps)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
@@ -475,7 +477,25 @@ def main():
         e2e_ms = torch.tensor([s0.elapsed_time(s1) / n_e2e], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+        # the link's floor for one step: the same uploads and download, concurrent, no compute
+        dq, dk, dv, dout = bufs[0]
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        f0.record(s_in)
+        s_out.wait_event(f0)
+        for _ in range(3):
+            with torch.cuda.stream(s_in):
+                dq.copy_(hq_, non_blocking=True)
+                dk.copy_(hk_, non_blocking=True)
+                dv.copy_(hv_, non_blocking=True)
+            with torch.cuda.stream(s_out):
+                hout.copy_(dout, non_blocking=True)
+        s_in.wait_stream(s_out)
+        f1.record(s_in)
+        torch.cuda.synchronize()
+        link_ms = f0.elapsed_time(f1) / 3
         e2e = {"value": round(float(e2e_ms), 3), "unit": UNIT,
+               "link_floor_ms": round(link_ms, 3),
                "h2d_bytes_per_step": int((q.numel() + k.numel() + v.numel()) * q.element_size() * world),
                "d2h_bytes_per_step": int(out.numel() * out.element_size() * world), "steps": n_e2e,
                "pipelined": "upload / compute / download on three streams, device buffers double-buffered"}
