@@ -11,6 +11,7 @@ from ._lib import FlashPrefillError
 from ._ops import check_device_error, get_mean_warps, search_dense, search_varlen, set_mean_warps
 from .flashprefill_native_forward import flash_prefill
 from .flashprefill_varlen_func import flash_prefill_varlen_func
+from . import torch_ops  # registers torch.ops.flashprefill.prefill_dense / prefill_varlen
 
 __all__ = ["flash_prefill", "flash_prefill_varlen_func", "search_dense", "search_varlen", "set_mean_warps",
            "get_mean_warps", "check_device_error", "FlashPrefillError", "install_as_ops"]
