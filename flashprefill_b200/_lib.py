@@ -51,6 +51,8 @@ SIGNATURES = {
     "fpb_attention_varlen": (_I, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I64P, _I64P, _I64P, _I64P,
                                   _I, _P, _SZ, _P]),
     "fpb_read_device_error": (_I, [_P, _U32P, _P]),
+    "fpb_noalloc_read_device_error": (_I, [_U32P, _P]),
+    "fpb_test_set_fault": (_I, [_I, ctypes.c_ulonglong]),
     "fpb_prefill_dense_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I64P, _I64P, _I64P, _I64P,
                                        _I, _I, _I, _F, _I, _I, _I, _P]),
 }

@@ -64,16 +64,30 @@ struct Layout {
 
 int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
+// Bounds that keep every workspace offset and kernel index in range: at most 2^30 query-block
+// rows (tiles) per call, and at most 2^34 list entries (hq * tiles * cap, 64 GiB of lists).
+constexpr int64_t kMaxTiles = int64_t(1) << 30;
+constexpr int64_t kMaxListEntries = int64_t(1) << 34;
+
+// Rejects sizes whose tile count or list area would leave those bounds.
+int check_tiles(int64_t tiles, int64_t cap, int hq) {
+  if (tiles >= kMaxTiles || (int64_t)hq * tiles * cap > kMaxListEntries)
+    return fail(FPB_EINVAL, "problem too large: %lld query-block rows x %lld blocks x %d heads", (long long)tiles,
+                (long long)cap, hq);
+  return FPB_OK;
+}
+
 // varlen=0: a=batch, b=seqlen; varlen=1: a=nseq, b=total_tokens, c=max_seq_len
 Layout make_layout(int varlen, int a, int b, int c, int hq, int hk) {
   Layout L{};
   const int nseq = a;
   if (!varlen) {
     const int nb = (b + kBlock - 1) / kBlock;
-    L.tiles = a * nb;
+    L.tiles = (int)std::min<int64_t>((int64_t)a * nb, kMaxTiles);  // callers reject more (check_tiles)
     L.cap = nb;
   } else {
-    L.tiles = (b + kBlock - 1) / kBlock + a;  // sum ceil(len_i/128) <= ceil(T/128) + nseq
+    // sum ceil(len_i/128) <= ceil(T/128) + nseq
+    L.tiles = (int)std::min<int64_t>((int64_t)(b + kBlock - 1) / kBlock + a, kMaxTiles);
     L.cap = (c + kBlock - 1) / kBlock;
     if (L.cap < 1) L.cap = 1;
   }
@@ -391,8 +405,9 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
     A.sp_counters = S.counters;
     A.sp_part = reinterpret_cast<float*>(ws + L.sp_part);
   }
-  A.profile = std::getenv("FLASHPREFILL_B200_PROFILE") != nullptr;
   A.alt_issue = std::getenv("FLASHPREFILL_B200_ISSUE") && std::strcmp(std::getenv("FLASHPREFILL_B200_ISSUE"), "alt") == 0;
+#if FPB_ATTN_PROFILE
+  A.profile = std::getenv("FLASHPREFILL_B200_PROFILE") != nullptr;
   A.trace = std::getenv("FLASHPREFILL_B200_TRACE") != nullptr;
   if (A.trace) {
     static const unsigned int zero = 0;
@@ -402,6 +417,10 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
     static const unsigned long long zeros[kProfSlots] = {};
     FPB_CUDA(cudaMemcpyToSymbolAsync(g_attn_prof, zeros, sizeof(zeros), 0, cudaMemcpyHostToDevice, stream));
   }
+#else
+  A.profile = 0;
+  A.trace = 0;
+#endif
   A.n_peers = n_peers;
   for (int i = 0; i < n_peers; ++i) A.peer_out[i] = out_peers[i];
   // the peer-writing instance only when there are peers: the plain one is the hot path
@@ -420,6 +439,7 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
   FPB_TRY(set_smem(kern, smem));
   kern<<<grid, kAttnThreads, smem, stream>>>(tm_q, tm_k, tm_v, tm_o, A);
   FPB_CUDA(cudaGetLastError());
+#if FPB_ATTN_PROFILE
   if (A.trace) {  // debug: CTA 0's event trace, written to the file the variable names
     unsigned int n = 0;
     FPB_CUDA(cudaMemcpyFromSymbolAsync(&n, g_attn_trace_n, sizeof(n), 0, cudaMemcpyDeviceToHost, stream));
@@ -444,6 +464,7 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
     fprintf(stderr, "[fpb profile] grid=%u\n", grid);
     for (int i = 0; i < kProfSlots; ++i) fprintf(stderr, "[fpb profile] %-26s %llu\n", names[i], h[i]);
   }
+#endif
   return FPB_OK;
 }
 
@@ -452,6 +473,10 @@ int check_dense(const void* q, const void* k, int dtype, int batch, int seqlen, 
   FPB_TRY(check_common(dtype, hq, hk, head_dim, block_size));
   FPB_CHECK_ARG(batch >= 1 && seqlen >= 1, "batch (%d) and seqlen (%d) must be >= 1", batch, seqlen);
   FPB_CHECK_ARG((int64_t)seqlen + kBlock < (int64_t(1) << 31), "seqlen too large");
+  {
+    const int64_t nb = ((int64_t)seqlen + kBlock - 1) / kBlock;
+    FPB_TRY(check_tiles((int64_t)batch * nb, nb, hq));
+  }
   FPB_TRY(check_ptr(q, "q"));
   FPB_TRY(check_ptr(k, "k"));
   FPB_TRY(check_strides(qs, 3, "q"));
@@ -472,6 +497,9 @@ int check_varlen(const void* q, const void* k, int dtype, const int32_t* cu, int
   FPB_TRY(check_common(dtype, hq, hk, head_dim, block_size));
   FPB_CHECK_ARG(nseq >= 1, "cu_seqlens must hold at least 2 entries");
   FPB_CHECK_ARG(total >= 0 && max_len >= 0, "total_tokens and max_seq_len must be >= 0");
+  FPB_CHECK_ARG((int64_t)total + kBlock < (int64_t(1) << 31) && (int64_t)max_len + kBlock < (int64_t(1) << 31),
+                "total_tokens or max_seq_len too large");
+  FPB_TRY(check_tiles(((int64_t)total + kBlock - 1) / kBlock + nseq, std::max<int64_t>(1, ((int64_t)max_len + kBlock - 1) / kBlock), hq));
   FPB_CHECK_ARG(cu != nullptr && (reinterpret_cast<uintptr_t>(cu) & 3) == 0,
                 "cu_seqlens must be an aligned int32 pointer");
   FPB_TRY(check_ptr(q, "q"));
@@ -685,6 +713,16 @@ int fpb_prefill_varlen(const void* q, const void* k, const void* v, void* o, int
   auto st = static_cast<cudaStream_t>(stream);
   FPB_TRY(run_search(g, q, k, qs, ks, attention_sink, window_size, alpha, last_n_block, 0, mean_model, ws, L, st));
   return run_attention(g, q, k, v, o, qs, ks, vs, os, ws, L, workspace_bytes, st);
+}
+
+int fpb_test_set_fault(int withhold_first_load, unsigned long long wait_limit_ns) {
+  FPB_CHECK_ARG(wait_limit_ns >= 1000000ull && wait_limit_ns <= kWaitLimitNs,
+                "wait_limit_ns must be in [1 ms, 1 s]");
+  const int w = withhold_first_load ? 1 : 0;
+  const uint64_t lim = wait_limit_ns;
+  FPB_CUDA(cudaMemcpyToSymbol(g_test_withhold, &w, sizeof(w)));
+  FPB_CUDA(cudaMemcpyToSymbol(g_wait_limit_ns, &lim, sizeof(lim)));
+  return FPB_OK;
 }
 
 int fpb_read_device_error(const void* workspace, uint32_t* flags, void* stream) {

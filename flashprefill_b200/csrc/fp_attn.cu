@@ -7,16 +7,17 @@
 // dtype for the P V product, O = acc / l stored in the input dtype.  A row whose list is
 // empty outputs zeros (the reference starts l at 1.0 and acc at 0).
 //
-// Persistent kernel, one CTA per SM, 384 threads, running two independent pipelines that
-// share the tensor core.  A work item is one (query block, query head); each pipeline
-// fetches its own items, heavy-first, from one atomic counter.
-//   warp 0 / warp 2   scheduler + TMA producer (Q, then K and V of each listed block)
-//                     of pipeline 0 / 1, with single-slot Q, K and V buffers
-//   warp 1            TMEM owner + tcgen05.mma issuer: a non-blocking state machine that
-//                     issues for whichever pipeline has its inputs ready (S_x(j) = Q K^T
-//                     when K_x(j) has landed; PV_x(j) when P_x(j) and V_x(j) are ready)
-//   warps 4-7 / 8-11  softmax / epilogue of pipeline 0 / 1; one TMEM lane (= one query
-//                     row) per thread
+// Persistent kernel, one CTA per SM, 640 threads (20 warps), running two independent
+// pipelines that share the tensor core.  A work item is one (query block, query head), or
+// one chunk of a long row (fp_split.cu); each pipeline fetches its own items, heavy-first,
+// from one atomic counter.
+//   warp 0 / warp 2    scheduler + TMA producer (Q, then K and V of each listed block)
+//                      of pipeline 0 / 1, with single-slot Q, K and V buffers
+//   warp 1 / warp 3    tcgen05.mma issuer of pipeline 0 / 1 (warp 1 owns the TMEM
+//                      allocation): S_x(j) = Q K^T when K_x(j) has landed, PV_x(j) when
+//                      P_x(j) and V_x(j) are ready
+//   warps 4-11 / 12-19 softmax / epilogue of pipeline 0 / 1: two warpgroups per pipeline,
+//                      thread (half hh, row r) owns 64 columns of query row r (= TMEM lane)
 // While one pipeline's softmax runs, the tensor core works for the other.  PV_x(j) is
 // issued before S_x(j+1), so O_x is final whenever S_x(j+1) completes: the exact
 // running-max rescale of O (as in the reference) never waits.
@@ -74,10 +75,20 @@ constexpr bool kSoftmaxProbe = FPB_SOFTMAX_PROBE;
 constexpr int kAttnLaunchRegs = 96, kAttnRoleRegs = 64, kAttnSoftmaxRegs = 104;
 static_assert(128 * kAttnRoleRegs + 512 * kAttnSoftmaxRegs <= kAttnThreads * kAttnLaunchRegs, "register split");
 
-// Opt-in instrumentation (FLASHPREFILL_B200_PROFILE=1): cycles spent per wait / phase,
-// summed over CTAs.  Indices: see kProfNames in fp_api.cu.
+// Instrumentation, compiled in only with -DFPB_ATTN_PROFILE=1 (build flag), then enabled at
+// run time by FLASHPREFILL_B200_PROFILE=1 (cycles spent per wait / phase, summed over CTAs;
+// indices: kProfNames in fp_api.cu) and FLASHPREFILL_B200_TRACE=<file> (event trace of CTA 0:
+// (clock, kind << 56 | a << 28 | b) pairs).  In the default build every hook below is empty
+// and no clock is read on the hot path.
+#ifndef FPB_ATTN_PROFILE
+#define FPB_ATTN_PROFILE 0
+#endif
 constexpr int kProfSlots = 25;
+constexpr int kTraceCap = 1 << 16;
+#if FPB_ATTN_PROFILE
 __device__ unsigned long long g_attn_prof[kProfSlots];
+__device__ unsigned long long g_attn_trace[2 * kTraceCap];
+__device__ unsigned int g_attn_trace_n;
 struct ProfAcc {  // counters live in shared memory, flushed once per CTA
   unsigned long long* sm;
   __device__ void add(int i, unsigned long long c) {
@@ -85,10 +96,6 @@ struct ProfAcc {  // counters live in shared memory, flushed once per CTA
   }
 };
 __device__ __forceinline__ unsigned long long clk() { return clock64(); }
-// Opt-in event trace of CTA 0: (clock, kind << 56 | a << 28 | b) pairs.
-constexpr int kTraceCap = 1 << 16;
-__device__ unsigned long long g_attn_trace[2 * kTraceCap];
-__device__ unsigned int g_attn_trace_n;
 #define trace(on, kind, a, b) trace_((on), trace_ctr, (kind), (a), (b))
 __device__ __forceinline__ void trace_(bool on, unsigned* ctr, uint32_t kind, uint32_t a, uint32_t b) {
   if (!on) return;
@@ -106,6 +113,15 @@ __device__ __forceinline__ void trace_(bool on, unsigned* ctr, uint32_t kind, ui
     pa.add(slot, clk() - t0_);               \
     r_;                                      \
   })
+#else
+struct ProfAcc {
+  unsigned long long* sm;
+  __device__ __forceinline__ void add(int, unsigned long long) {}
+};
+__device__ __forceinline__ unsigned long long clk() { return 0; }
+#define trace(on, kind, a, b) ((void)0)
+#define FPB_TW(slot, call) (call)
+#endif
 constexpr uint32_t kAttnTile = 128 * 128 * 2;
 constexpr uint32_t kAttnHalf = kAttnTile / 2;
 
@@ -316,6 +332,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // chunks of split rows come first in the work order (they are the longest work)
     const int n_ent = A.split ? A.sp_head[0] : 0;
     const int split_thr = A.split ? A.sp_head[3] : 0x7fffffff;  // only rows above it can be split
+    // test hook: CTA 0's pipeline 0 withholds its first key load, so its MMA issuer's wait runs out
+    const bool withhold = blockIdx.x == 0 && x == 0 && *(volatile int*)&g_test_withhold != 0;
     bool ok = true;
     while (ok) {
       const int slot = it & 1;
@@ -378,9 +396,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (!FPB_TW(13, mbar_wait_sleep(k_empty + x, (kseq & 1) ^ 1, abort))) { ok = false; break; }
         trace(tr, 1, x, kseq);
         ++kseq;
-        mbar_arrive_expect_tx(k_full + x, kAttnTile);
-        tma_load_4d(sK, &tm_k, k_full + x, 0, hk, krow, f.bcoord);
-        tma_load_4d(sK + kAttnHalf, &tm_k, k_full + x, 64, hk, krow, f.bcoord);
+        if (!(withhold && kseq == 1)) {
+          mbar_arrive_expect_tx(k_full + x, kAttnTile);
+          tma_load_4d(sK, &tm_k, k_full + x, 0, hk, krow, f.bcoord);
+          tma_load_4d(sK + kAttnHalf, &tm_k, k_full + x, 64, hk, krow, f.bcoord);
+        }
         if (!FPB_TW(16, mbar_wait_sleep(v_empty + x, (vseq & 1) ^ 1, abort))) { ok = false; break; }
         if (j == 0 && qld > 1) {  // the previous item's epilogue stages its output in the V tile
           if (!FPB_TW(16, mbar_wait_sleep(stage_free + x, sfc & 1, abort))) { ok = false; break; }
@@ -492,7 +512,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       if (progress) {
         last_progress = global_timer_ns();
-      } else if (*abort || global_timer_ns() - last_progress > kWaitLimitNs) {
+      } else if (*abort || global_timer_ns() - last_progress > g_wait_limit_ns) {
         *abort = 1;
         break;
       }
@@ -801,8 +821,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (threadIdx.x == 0) pa.add(18, clk() - t_kernel0);
   tc_fence_before();
   __syncthreads();
+#if FPB_ATTN_PROFILE
   if (A.profile && threadIdx.x < kProfSlots) atomicAdd(&g_attn_prof[threadIdx.x], prof_smem[threadIdx.x]);
   if (tr && threadIdx.x == 0) g_attn_trace_n = *trace_ctr;
+#endif
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);

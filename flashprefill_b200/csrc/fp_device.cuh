@@ -17,6 +17,11 @@ namespace fpb {
 
 // A single wait never legitimately lasts longer than this; 1 s of global time.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
+// The limit the kernels apply (kWaitLimitNs unless a test shortens it through
+// fpb_test_set_fault), and the test hook that makes CTA 0 of the attention kernel withhold
+// its first key load so that a wait runs out.  Both are set from the host only.
+__device__ uint64_t g_wait_limit_ns = kWaitLimitNs;
+__device__ int g_test_withhold;
 #ifndef FPB_SLEEP_HINT_NS
 #define FPB_SLEEP_HINT_NS 20000
 #endif
@@ -90,11 +95,11 @@ __device__ __forceinline__ bool mbar_probe(uint64_t* bar, uint32_t parity) {
 // when another thread of the CTA has raised *abort (the CTA is shutting down).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_test(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
+  const uint64_t t0 = global_timer_ns(), lim = g_wait_limit_ns;
   while (true) {
     if (mbar_test(bar, parity)) return true;
     if (*abort) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > lim) {
       *abort = 1;
       return false;
     }
@@ -104,21 +109,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // Bounded wait that sleeps between polls (for waits that are usually long).
 __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_test_sleep(bar, parity, kSleepHintNs)) return true;
-  const uint64_t t0 = global_timer_ns();
+  const uint64_t t0 = global_timer_ns(), lim = g_wait_limit_ns;
   while (true) {
     if (mbar_test_sleep(bar, parity, kSleepHintNs)) return true;
     if (*abort) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > lim) {
       *abort = 1;
       return false;
     }
   }
 }
 __device__ __forceinline__ bool mbar_wait_warp_sleep(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  const uint64_t t0 = global_timer_ns();
+  const uint64_t t0 = global_timer_ns(), lim = g_wait_limit_ns;
   while (true) {
     if (__all_sync(0xffffffffu, mbar_test_sleep(bar, parity, kSleepHintNs))) return true;
-    const bool stop = (*abort != 0) || (global_timer_ns() - t0 > kWaitLimitNs);
+    const bool stop = (*abort != 0) || (global_timer_ns() - t0 > lim);
     if (__any_sync(0xffffffffu, stop)) {
       *abort = 1;
       return false;
@@ -130,11 +135,11 @@ __device__ __forceinline__ bool mbar_wait_warp_sleep(uint64_t* bar, uint32_t par
 // (tcgen05.ld/st, shuffles): every lane returns the same value.
 template <bool kProbe = false>
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  const uint64_t t0 = global_timer_ns();
+  const uint64_t t0 = global_timer_ns(), lim = g_wait_limit_ns;
   while (true) {
     const bool done = kProbe ? mbar_probe(bar, parity) : mbar_test(bar, parity);
     if (__all_sync(0xffffffffu, done)) return true;
-    const bool stop = (*abort != 0) || (global_timer_ns() - t0 > kWaitLimitNs);
+    const bool stop = (*abort != 0) || (global_timer_ns() - t0 > lim);
     if (__any_sync(0xffffffffu, stop)) {
       *abort = 1;
       return false;

@@ -45,6 +45,14 @@ int noalloc_scratch(void** out) {
 }  // namespace
 }  // namespace fpb
 
+extern "C" int fpb_noalloc_read_device_error(uint32_t* flags, void* stream) {
+  using namespace fpb;
+  FPB_CHECK_ARG(flags != nullptr, "flags is NULL");
+  void* ws = nullptr;
+  FPB_TRY(noalloc_scratch(&ws));
+  return fpb_read_device_error(ws, flags, stream);
+}
+
 extern "C" int fpb_prefill_dense_noalloc(const void* q, const void* k, const void* v, void* out, int dtype,
                                          int batch, int seqlen, int hq, int hk, int head_dim,
                                          const int64_t* q_strides, const int64_t* k_strides,
@@ -53,6 +61,7 @@ extern "C" int fpb_prefill_dense_noalloc(const void* q, const void* k, const voi
                                          int min_budget, int mean_model, void* stream) {
   using namespace fpb;
   FPB_CHECK_ARG(batch >= 1 && seqlen >= 1 && hq >= 1 && hk >= 1, "batch, seqlen and head counts must be >= 1");
+  FPB_TRY(check_dense(q, k, dtype, batch, seqlen, hq, hk, head_dim, q_strides, k_strides, block_size));
   const Layout L = make_layout(0, batch, seqlen, 0, hq, hk);
   // the required part of the workspace must fit; the optional long-row split area is used
   // only where it fits as well

@@ -15,11 +15,16 @@ patches/patch_loader_vllm_0_10_0.py).  Those loaders import modules the installe
 * every other batch (decode steps, cached prefixes, mixed prefill/decode batches, profiling
   runs with no metadata) runs the original ``forward`` unchanged.
 
-The last condition is checked on the device.  Its result is read back once per batch whose
-``max_query_len`` exceeds 1 (one host sync per layer of a prefill step).  The reference
-instead takes any batch with ``max_query_len > 1`` as a prefill
-(patch_loader_vllm_0_12_0.py:167-168), which computes wrong attention for the decode tokens
-and cached prefixes such a batch can hold.
+The last condition is decided on the host, without a device sync: the patch also wraps
+``FlashAttentionMetadataBuilder.build``, which vLLM calls once per batch with the
+scheduler's host-side copies of the query start offsets (``query_start_loc_cpu``) and
+sequence lengths (``seq_lens_cpu_upper_bound``, exact for prefill rows and never below the
+real length); it stores the verdict on the metadata it returns (``fp_whole_prefill``).
+A query length equal to the upper bound of its sequence length means the sequence has no
+cached prefix.  Metadata without that verdict, and batches traced during CUDA-graph
+capture, run vLLM's own ``forward``.  The reference instead takes any batch with
+``max_query_len > 1`` as a prefill (patch_loader_vllm_0_12_0.py:167-168), which computes
+wrong attention for the decode tokens and cached prefixes such a batch can hold.
 
 Usage, in every worker process before the model runs::
 
@@ -41,7 +46,7 @@ ATTENTION_CONFIGS = {
                               "last_n_full_block": 2},
 }
 
-_state = {"original": None, "cfg": None, "calls": 0, "fallbacks": 0}
+_state = {"original": None, "original_build": None, "cfg": None, "calls": 0, "fallbacks": 0}
 
 
 def _backend():
@@ -71,17 +76,42 @@ def _static_ok(impl, query, output_scale, output_block_scale) -> bool:
     return query.dtype in (torch.bfloat16, torch.float16)
 
 
+def whole_prefill_from_host(common) -> bool | None:
+    """Host-side verdict for one batch (CommonAttentionMetadata): True when every sequence is a
+    new prefill (query length == sequence length), None when the host copies are missing."""
+    qsl = getattr(common, "query_start_loc_cpu", None)
+    sl = getattr(common, "seq_lens_cpu_upper_bound", None)
+    if sl is None:
+        sl = getattr(common, "_seq_lens_cpu", None)
+    if qsl is None or sl is None:
+        return None
+    n = int(common.num_reqs)
+    if n < 1 or int(common.max_query_len) <= 1:
+        return False
+    q_lens = qsl[1:n + 1] - qsl[:n]
+    return bool((q_lens.to(sl.dtype) == sl[:n]).all())
+
+
 def _whole_prefills(attn_metadata) -> bool:
     """True when every sequence of the batch is a new prefill: query length == KV length.
-    Reads one device flag back (a host sync)."""
+    Uses only host data (the verdict the wrapped metadata builder attached)."""
+    import torch
     if attn_metadata.use_cascade or attn_metadata.max_query_len <= 1:
         return False
     if attn_metadata.max_seq_len != attn_metadata.max_query_len:
         return False  # some sequence has KV beyond its queries
-    qsl = attn_metadata.query_start_loc
-    nseq = attn_metadata.seq_lens.shape[0]
-    q_lens = qsl[1:nseq + 1] - qsl[:nseq]
-    return bool((q_lens == attn_metadata.seq_lens[:nseq]).all())
+    if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
+        return False  # a captured graph would freeze this batch's routing
+    return getattr(attn_metadata, "fp_whole_prefill", None) is True
+
+
+def _build(self, common_prefix_len, common_attn_metadata, *args, **kwargs):
+    md = _state["original_build"](self, common_prefix_len, common_attn_metadata, *args, **kwargs)
+    try:
+        md.fp_whole_prefill = whole_prefill_from_host(common_attn_metadata)
+    except Exception:  # metadata of an unexpected shape: leave the verdict unset (fallback)
+        pass
+    return md
 
 
 def _prefill(query, key, value, output, attn_metadata, cfg) -> None:
@@ -118,15 +148,19 @@ def apply_patch_to_worker(worker=None, config: str | dict = "flashprefill_llama"
     fa = _backend()
     if _state["original"] is None:
         _state["original"] = fa.FlashAttentionImpl.forward
+        _state["original_build"] = fa.FlashAttentionMetadataBuilder.build
     _state["cfg"] = cfg
     fa.FlashAttentionImpl.forward = _forward
+    fa.FlashAttentionMetadataBuilder.build = _build
 
 
 def remove_patch() -> None:
     """Restore vLLM's own FlashAttentionImpl.forward."""
     if _state["original"] is not None:
         _backend().FlashAttentionImpl.forward = _state["original"]
+        _backend().FlashAttentionMetadataBuilder.build = _state["original_build"]
         _state["original"] = None
+        _state["original_build"] = None
         _state["cfg"] = None
 
 

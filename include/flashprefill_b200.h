@@ -152,17 +152,33 @@ FPB_API int fpb_attention_varlen(const void* q, const void* k, const void* v, vo
  * a workspace (runtimes that forbid allocation on their hot path, hosts without a device
  * allocator).  No counterpart in the reference.  Same arguments and results as
  * fpb_prefill_dense without the workspace: it uses a 32 MiB device array inside the
- * library, held by every GPU that loads the library until exit.  Problems whose
- * workspace (fpb_dense_workspace_bytes) exceeds 32 MiB are rejected with FPB_EINVAL
- * (e.g. 32K tokens with 32/8 heads fit; 128K do not).  The first call on a device looks
- * up the array's address on that device and should come before any stream capture.
- * Calls share the array: calls that overlap on the GPU race. */
+ * library, held by every GPU that loads the library until exit.  Problems whose required
+ * workspace (the error word, pooled keys, counts and block lists: every part of
+ * fpb_dense_workspace_bytes except the optional long-row split area) exceeds 32 MiB are
+ * rejected with FPB_EINVAL (e.g. 32K tokens with 32/8 heads fit; 128K do not); long rows
+ * are split only when the split area fits in the array as well.  The first call on a
+ * device looks up the array's address on that device and should come before any stream
+ * capture.  Calls share the array: calls that overlap on the GPU race.  Device-side errors
+ * of these calls are read with fpb_noalloc_read_device_error. */
 FPB_API int fpb_prefill_dense_noalloc(const void* q, const void* k, const void* v, void* out, int dtype, int batch,
                                       int seqlen, int hq, int hk, int head_dim, const int64_t* q_strides,
                                       const int64_t* k_strides, const int64_t* v_strides,
                                       const int64_t* o_strides, int block_size, int attention_sink,
                                       int window_size, float alpha, int last_n_block_full, int min_budget,
                                       int mean_model, void* stream);
+
+/* fpb_read_device_error for the no-allocation path: synchronises `stream` and reads the
+ * error word of the current device's fixed scratch array (the last
+ * fpb_prefill_dense_noalloc call on that device).  No counterpart in the reference. */
+FPB_API int fpb_noalloc_read_device_error(uint32_t* flags, void* stream);
+
+/* Test hook, no counterpart in the reference: on the current device, sets the limit of every
+ * bounded device-side wait (default 1 s; accepted range 1 ms .. 1 s) and, when
+ * withhold_first_load is non-zero, makes the attention kernel's first CTA skip its first
+ * key-tile load, so that one of its waits runs out and the call reports
+ * FPB_DEV_WAIT_TIMEOUT through the error word.  Call it again with (0, 1000000000) to
+ * restore normal operation.  For tests of the timeout path only. */
+FPB_API int fpb_test_set_fault(int withhold_first_load, unsigned long long wait_limit_ns);
 
 /* Synchronises `stream`, copies the device error word of `workspace` to *flags and
  * returns FPB_EDEVICE if any bit is set.  No counterpart in the reference, which has no

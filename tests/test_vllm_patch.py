@@ -20,11 +20,21 @@ def _impl(**kw):
     return SimpleNamespace(**d)
 
 
-def _meta(q_lens, kv_lens, cascade=False):
+def _common(q_lens, kv_lens, upper=None):
+    """CommonAttentionMetadata stand-in with the host copies vLLM's scheduler provides."""
     qsl = torch.tensor([0] + list(torch.tensor(q_lens).cumsum(0)), dtype=torch.int32)
-    return SimpleNamespace(num_actual_tokens=int(sum(q_lens)), max_query_len=max(q_lens), query_start_loc=qsl,
-                           max_seq_len=max(kv_lens), seq_lens=torch.tensor(kv_lens, dtype=torch.int32),
-                           use_cascade=cascade)
+    return SimpleNamespace(num_reqs=len(q_lens), max_query_len=max(q_lens), query_start_loc_cpu=qsl,
+                           seq_lens_cpu_upper_bound=torch.tensor(upper or kv_lens, dtype=torch.int32))
+
+
+def _meta(q_lens, kv_lens, cascade=False, verdict="host"):
+    qsl = torch.tensor([0] + list(torch.tensor(q_lens).cumsum(0)), dtype=torch.int32)
+    m = SimpleNamespace(num_actual_tokens=int(sum(q_lens)), max_query_len=max(q_lens), query_start_loc=qsl,
+                        max_seq_len=max(kv_lens), seq_lens=torch.tensor(kv_lens, dtype=torch.int32),
+                        use_cascade=cascade)
+    if verdict == "host":  # what the wrapped metadata builder attaches
+        m.fp_whole_prefill = vp.whole_prefill_from_host(_common(q_lens, kv_lens))
+    return m
 
 
 @pytest.fixture
@@ -70,15 +80,53 @@ def test_whole_prefills_go_sparse(patched):
     assert meta is m and cfg["alpha"] == 0.08 and o.shape == (m.num_actual_tokens + 3, 4, 128)
 
 
-@pytest.mark.parametrize("case", ["decode", "prefix", "mixed", "cascade", "profiling"])
+@pytest.mark.parametrize("case", ["decode", "prefix", "mixed", "cascade", "profiling", "no_verdict",
+                                  "prefix_same_max"])
 def test_other_batches_fall_back(patched, case):
     m = {"decode": _meta([1, 1], [500, 77]),
          "prefix": _meta([200], [700]),
          "mixed": _meta([1000, 1], [1000, 40]),
          "cascade": _meta([300, 300], [300, 300], cascade=True),
-         "profiling": None}[case]
+         "profiling": None,
+         # metadata not made by the wrapped builder: no host verdict, so no sparse prefill
+         "no_verdict": _meta([300], [300], verdict=None),
+         # equal maxima, but the second sequence has a cached prefix (host check per sequence)
+         "prefix_same_max": _meta([1000, 200], [1000, 700])}[case]
     _call(_impl(), m)
     assert not patched["sparse"] and len(patched["orig"]) == 1
+
+
+def test_host_verdict():
+    assert vp.whole_prefill_from_host(_common([300, 129], [300, 129])) is True
+    assert vp.whole_prefill_from_host(_common([300, 1], [300, 40])) is False
+    # an upper bound above the real length (async speculative decode) never passes as a prefill
+    assert vp.whole_prefill_from_host(_common([300, 5], [300, 5], upper=[300, 9])) is False
+    assert vp.whole_prefill_from_host(_common([1, 1], [1, 1])) is False  # max_query_len 1: decode
+    assert vp.whole_prefill_from_host(SimpleNamespace(num_reqs=1, max_query_len=4)) is None
+
+
+def test_builder_wrapper_attaches_the_verdict(patched, monkeypatch):
+    made = SimpleNamespace()
+    monkeypatch.setitem(vp._state, "original_build", lambda self, cpl, common, *a, **kw: made)
+    md = vp._build(None, 0, _common([300], [300]))
+    assert md is made and md.fp_whole_prefill is True
+    md = vp._build(None, 0, _common([300], [700]))
+    assert md.fp_whole_prefill is False
+
+
+def test_capture_falls_back(patched, monkeypatch):
+    """A batch traced while a CUDA graph is being captured keeps vLLM's own forward."""
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: True)
+    monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: True)
+    _call(_impl(), _meta([300], [300]))
+    assert not patched["sparse"] and len(patched["orig"]) == 1
+
+
+def test_no_device_reads_in_dispatch():
+    """The dispatch path holds no .item() / bool(tensor) host syncs on device data."""
+    import inspect
+    src = inspect.getsource(vp._whole_prefills) + inspect.getsource(vp._forward)
+    assert ".item()" not in src and ".all()" not in src
 
 
 @pytest.mark.parametrize("kw", [dict(sliding_window=(1023, 0)), dict(alibi_slopes=torch.zeros(4)),
