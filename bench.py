@@ -5,9 +5,10 @@
 
 Default workload: the 128K-token Llama-3-8B-shaped layer the headline metric is quoted on
 (S=131072, 32 query / 8 KV heads, head_dim 128, bf16, alpha 0.18, sink 2, window 4,
-last_n 2).  Under torchrun (N>1) each rank owns a contiguous group of KV heads (and their
-query heads) of the SAME layer -- heads shard with no cross-GPU dependency -- so total work
-is fixed and the reported ms/layer is the max over ranks ("scaling": "strong").
+last_n 2).  Under torchrun (N>1) every rank generates the same seeded layer and keeps a
+contiguous group of KV heads (and their query heads) -- heads shard with no cross-GPU
+dependency -- so total work is fixed and the reported ms/layer is the max over ranks
+("scaling": "strong").
 
 Timed region (``value``): K steps of the operator on inputs already in HBM (1.6 GB at
 128K, larger than the 126 MB L2, so no extra flush), CUDA events on the launching stream,
@@ -15,13 +16,21 @@ barrier + synchronize on both sides, max over ranks.  ``e2e``: the same step thr
 public API ``flash_prefill`` with the inputs copied from pinned host memory and the output
 copied back inside the timed region.  ``roofline``: the attention kernel (dominant) against
 the measured dense bf16 peak; ``roofline_search``: the search stage against measured HBM
-bandwidth.  ``cpu_baseline``: the CPU restatement (oracle) on a bounded sample of the same
-layer, extrapolated to the whole layer.
+bandwidth.
 
-``--impl reference``: the reference implementation has no CPU path of its own (its Triton
-kernels only run on CPU through the interpreter, and its sources are not shipped to the
-GPU host), so this arm times the CPU restatement of the reference algorithm (``oracle/``)
-with every host thread on a bounded sample of the same layer, extrapolated to ms/layer.
+Baselines (rank 0, N=1), none of them on the product path:
+  ``triton_baseline``: the reference's own Triton implementation (qhfan/FlashPrefill ops/,
+      staged unmodified by oracle/stage_ref.py) on this GPU, same inputs, autotune warmed;
+      with the comparison of its block masks and pooled keys with ours;
+  ``cpu_baseline``: the CPU restatement (oracle) on a bounded sample of the same layer,
+      extrapolated to the whole layer;
+  ``cpu_baseline_interpreter``: the reference's own kernels under the Triton interpreter on
+      the host, one complete BASELINE configs[0] layer (fp32, S=4096), not extrapolated.
+
+``--impl reference``: the reference has no CPU implementation of its own (its Triton kernels
+run on the host only through the interpreter, far too slowly for this layer), so this arm
+times the CPU restatement of the reference algorithm (``oracle/``) with every host thread on
+a bounded sample of the same layer, extrapolated to ms/layer (``"extrapolated": true``).
 """
 from __future__ import annotations
 
@@ -251,7 +260,8 @@ def cpu_sample(w, seconds_budget=20.0):
     E_est = dens * total_rows
     ms = 1e3 * (t_mean * w.hk * (sum(w.seqlens) / L) + t_search / done * total_rows
                 + (t_attn / max(1, pairs)) * E_est)
-    info = {"sample": f"KV head 0 + its {G} query heads of one {L}-token sequence: pooled keys of all {nb} "
+    info = {"sample_seconds": t_mean + t_search + t_attn,
+            "sample": f"KV head 0 + its {G} query heads of one {L}-token sequence: pooled keys of all {nb} "
                       f"blocks, search on {done} random query blocks of one head, attention on {pairs} block "
                       f"pairs; extrapolated to {total_rows} (head, block) rows and E~{int(E_est)} pairs",
             "cores": os.cpu_count(),
@@ -283,6 +293,89 @@ def mask_exactness(w, sample, dev):
             "sample": "the CPU baseline's rows (query head 0 of KV head 0, one sequence, same inputs)"}
 
 
+def triton_baseline(w, q, k, v, cu, maxlen, ws, L, steps, ours_ms):
+    """Time the reference's Triton path (qhfan/FlashPrefill ops/, staged unmodified by
+    oracle/stage_ref.py) on this GPU on the same inputs, and compare its block masks with the
+    lists our last search left in ``ws``.  Not part of the product path."""
+    import torch
+
+    try:
+        from oracle import triton_ref as tr
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"import failed: {e}"}
+    if not tr.available():
+        return {"unavailable": "reference sources not staged (oracle/stage_ref.py) or triton/fla missing"}
+    from flashprefill_b200 import _ops
+    hq, hk = q.shape[1], k.shape[1]
+    cnt = ws[L["cnt"]:L["cnt"] + 4 * hq * L["tiles"]].view(torch.int32).view(hq, L["tiles"])
+    idx = ws[L["idx"]:L["idx"] + 4 * hq * L["tiles"] * L["cap"]].view(torch.int32).view(hq, L["tiles"], L["cap"])
+    ref_out = torch.zeros_like(q)
+    t0 = time.perf_counter()
+    if w.varlen:
+        call = lambda: tr.flash_prefill_varlen_func(q, k, v, ref_out, cu, maxlen, w.alpha, 128, 2, 4, 2)
+        st = tr.run_varlen(q, k, v, ref_out, cu, maxlen, w.alpha, 128, 2, 4, 2)
+        mk = ws[L["mk"]:L["mk"] + 2 * st["mk"].numel()].view(q.dtype).view(st["mk"].shape)
+        rep = tr.varlen_mask_diff(st, cnt, idx, w.seqlens, w.alpha)
+    else:
+        q4, k4, v4, o4 = q[None], k[None], v[None], ref_out[None]
+        call = lambda: tr.flash_prefill(q4, k4, v4, o4, 128, 2, 4, w.alpha, 2, 0)
+        st = tr.run_dense(q4, k4, v4, o4, 128, 2, 4, w.alpha, 2, 0)
+        mk = ws[L["mk"]:L["mk"] + 2 * st["mk"].numel()].view(q.dtype).view(st["mk"].shape)
+        rep = tr.dense_mask_diff(st, cnt, idx, w.alpha)
+    torch.cuda.synchronize()
+    first_s = time.perf_counter() - t0
+    mk_equal = bool(torch.equal(mk, st["mk"]))
+    warps = st["mean_warps"]
+    del st
+    ours_out = torch.empty_like(q)
+    if w.varlen:
+        _ops.prefill_varlen(q, k, v, ours_out, cu, maxlen, w.alpha, 128, 2, 4, 2)
+    else:
+        _ops.prefill_dense(q[None], k[None], v[None], ours_out[None], 128, 2, 4, w.alpha, 2, 0)
+    torch.cuda.synchronize()
+    d = (ours_out.float() - ref_out.float()).abs()
+    dmax, dmean = d.max().item(), d.mean().item()
+    del d, ours_out
+    for _ in range(2):
+        call()
+    stream = torch.cuda.current_stream()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    torch.cuda.synchronize()
+    for e0, e1 in evs:
+        e0.record(stream)
+        call()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    t = sorted(e0.elapsed_time(e1) for e0, e1 in evs)
+    ref_ms = sum(t) / len(t)
+    torch.cuda.empty_cache()
+    return {"value": round(ref_ms, 4), "unit": UNIT, "median_ms": round(t[len(t) // 2], 4), "steps": steps,
+            "ours_ms": round(ours_ms, 4), "speedup": round(ref_ms / ours_ms, 3),
+            "what": "reference ops.flash_prefill / flash_prefill_varlen_func (Triton, unmodified) on this GPU, "
+                    "same inputs, autotune cache warmed, CUDA events per call",
+            "first_call_s": round(first_s, 1), "mean_warps_autotuned": warps,
+            "pooled_keys_bit_identical": mk_equal,
+            "masks": {**rep, "rule": "ours vs the reference's lists; near = reference score within 1e-3 "
+                                     "relative of its row threshold"},
+            "output_vs_reference": {"max_abs": dmax, "mean_abs": dmean}}
+
+
+def interpreter_baseline():
+    """The reference's own kernels under the Triton interpreter on the host cores, one whole
+    cfg0 layer (fp32), timed end to end (oracle/interp_ref.py)."""
+    path = os.path.join(ROOT, "oracle", "interp_ref.py")
+    try:
+        r = subprocess.run([sys.executable, path], capture_output=True, text=True, timeout=600,
+                           env={**os.environ, "CUDA_VISIBLE_DEVICES": ""})
+        d = json.loads(r.stdout.strip().splitlines()[-1])
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"interpreter run failed: {e}"}
+    return {"value": round(d["seconds"] * 1e3, 1), "unit": UNIT, "cores": d["threads"], "kind": "reference",
+            "workload": "cfg0_dense_4k_fp32 (S=4096, 4/1 heads, fp32)", "extrapolated": False,
+            "sample": "the complete cfg0 layer: the reference's Triton kernels under TRITON_INTERPRET=1 on the "
+                      f"host, {d['selected_blocks']} blocks selected"}
+
+
 # --------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -293,6 +386,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-triton", action="store_true",
+                    help="skip the reference's Triton path on this GPU (timed baseline + mask comparison)")
     ap.add_argument("--no-gather", action="store_true",
                     help="N>1: skip the separately timed gathers of the head shards into the full output")
     ap.add_argument("--shard", default=None, help="R/N: run rank R's share of an N-GPU job alone on one GPU "
@@ -318,7 +413,9 @@ def main():
                 "cpu_baseline": {"value": round(ms, 3), "unit": UNIT, "cores": info["cores"], "kind": "port",
                                  "sample": info["sample"]},
                 "e2e": {"value": round(ms, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-                "note": "the reference has no CPU path of its own; this is the CPU restatement of its algorithm"}
+                "extrapolated": True, "sample_seconds": round(info["sample_seconds"], 2),
+                "note": "the reference has no CPU path of its own; this is the CPU restatement of its algorithm "
+                        "timed on a bounded sample of the layer and extrapolated to the whole layer"}
         print(json.dumps(line))
         return
 
@@ -342,7 +439,11 @@ def main():
         raise SystemExit(str(e))
     hq_l, hk_l = hq1 - hq0, hk1 - hk0
 
-    q, k, v = device_inputs(w, hk0, hk1, dev, seed=w.config_index * 1000 + 1 + hk0)
+    # every rank generates the same seeded layer and keeps its heads, so any N times the same layer
+    q, k, v = device_inputs(w, 0, w.hk, dev, seed=w.config_index * 1000 + 1)
+    if (hq0, hq1) != (0, w.hq):
+        q, k, v = q[:, hq0:hq1].contiguous(), k[:, hk0:hk1].contiguous(), v[:, hk0:hk1].contiguous()
+        torch.cuda.empty_cache()
     T = q.shape[0]
     cu = torch.tensor([0] + torch.tensor(w.seqlens).cumsum(0).tolist(), dtype=torch.int32, device=dev)
     maxlen = max(w.seqlens)
@@ -572,6 +673,15 @@ def main():
         if not w.varlen:
             exact = mask_exactness(w, info["mask_sample"], dev)
 
+    # ---- the reference's own Triton path on this GPU (rank 0, N=1): the bar to beat, and
+    # the reference's block masks compared with ours on the same inputs
+    triton = None
+    if rank == 0 and world == 1 and not shard and not a.no_triton:
+        triton = triton_baseline(w, q, k, v, cu, maxlen, ws, L, a.steps, ms)
+    interp = None
+    if rank == 0 and world == 1 and not a.no_cpu:
+        interp = interpreter_baseline()
+
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
@@ -612,6 +722,7 @@ def main():
             "search_ms": round(t_s, 4), "attention_ms": round(t_a, 4),
             "executed_pairs": E_total, "density": round(E_total / P_pairs, 5),
             "roofline": roof, "roofline_search": roof_s, "e2e": e2e, "cpu_baseline": cpu,
+            "cpu_baseline_interpreter": interp, "triton_baseline": triton,
             "mask_exactness": exact,
             "gpu_launches": a.steps * launches, "output_gather": gather,
             "clocks": clocks, "wall_s_timed": round(t_wall, 3)}

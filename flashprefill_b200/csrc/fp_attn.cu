@@ -332,8 +332,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // chunks of split rows come first in the work order (they are the longest work)
     const int n_ent = A.split ? A.sp_head[0] : 0;
     const int split_thr = A.split ? A.sp_head[3] : 0x7fffffff;  // only rows above it can be split
-    // test hook: CTA 0's pipeline 0 withholds its first key load, so its MMA issuer's wait runs out
-    const bool withhold = blockIdx.x == 0 && x == 0 && *(volatile int*)&g_test_withhold != 0;
     bool ok = true;
     while (ok) {
       const int slot = it & 1;
@@ -396,7 +394,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (!FPB_TW(13, mbar_wait_sleep(k_empty + x, (kseq & 1) ^ 1, abort))) { ok = false; break; }
         trace(tr, 1, x, kseq);
         ++kseq;
-        if (!(withhold && kseq == 1)) {
+        // test hook (one-shot): the first producer to reach a key load while it is armed skips
+        // that load, so its MMA issuer's wait runs out
+        bool withhold = false;
+        if (kseq == 1 && *(volatile int*)&g_test_withhold != 0) withhold = atomicExch(&g_test_withhold, 0) != 0;
+        if (!withhold) {
           mbar_arrive_expect_tx(k_full + x, kAttnTile);
           tma_load_4d(sK, &tm_k, k_full + x, 0, hk, krow, f.bcoord);
           tma_load_4d(sK + kAttnHalf, &tm_k, k_full + x, 64, hk, krow, f.bcoord);

@@ -18,8 +18,8 @@ namespace fpb {
 // A single wait never legitimately lasts longer than this; 1 s of global time.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 // The limit the kernels apply (kWaitLimitNs unless a test shortens it through
-// fpb_test_set_fault), and the test hook that makes CTA 0 of the attention kernel withhold
-// its first key load so that a wait runs out.  Both are set from the host only.
+// fpb_test_set_fault), and the one-shot test hook that makes the next attention launch skip
+// one key load so that a wait runs out (the producer that consumes it clears it).
 __device__ uint64_t g_wait_limit_ns = kWaitLimitNs;
 __device__ int g_test_withhold;
 #ifndef FPB_SLEEP_HINT_NS

@@ -174,10 +174,11 @@ FPB_API int fpb_noalloc_read_device_error(uint32_t* flags, void* stream);
 
 /* Test hook, no counterpart in the reference: on the current device, sets the limit of every
  * bounded device-side wait (default 1 s; accepted range 1 ms .. 1 s) and, when
- * withhold_first_load is non-zero, makes the attention kernel's first CTA skip its first
- * key-tile load, so that one of its waits runs out and the call reports
- * FPB_DEV_WAIT_TIMEOUT through the error word.  Call it again with (0, 1000000000) to
- * restore normal operation.  For tests of the timeout path only. */
+ * withhold_first_load is non-zero, arms a one-shot fault: the next attention launch on the
+ * device skips one key-tile load (the first producer to reach one consumes the fault), so
+ * that one of its waits runs out and the call reports FPB_DEV_WAIT_TIMEOUT through the
+ * error word.  Call it again with (0, 1000000000) to restore normal operation.  For tests
+ * of the timeout path only. */
 FPB_API int fpb_test_set_fault(int withhold_first_load, unsigned long long wait_limit_ns);
 
 /* Synchronises `stream`, copies the device error word of `workspace` to *flags and
