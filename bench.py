@@ -432,12 +432,18 @@ def main():
                                 timeout=datetime.timedelta(seconds=120))
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
-    from flashprefill_b200.sharding import head_shard
+    from flashprefill_b200.sharding import layer_shard
+    nb_max = math.ceil(max(w.seqlens) / 128)
+    r_, n_ = shard if shard else (rank, world)
+    if w.varlen and n_ > w.hk:
+        raise SystemExit(f"varlen workloads shard by KV head only ({w.hk} KV heads, {n_} ranks)")
     try:
-        hk0, hk1, hq0, hq1 = head_shard(w.hq, w.hk, *(shard if shard else (rank, world)))
+        hk0, hk1, hq0, hq1, qb0, qb1 = layer_shard(w.hq, w.hk, nb_max, r_, n_)
     except ValueError as e:
         raise SystemExit(str(e))
     hq_l, hk_l = hq1 - hq0, hk1 - hk0
+    # 2-D split (more ranks than KV heads): this rank runs query blocks [qb0, qb1) of its heads
+    rows2d = (qb0, qb1) != (0, nb_max)
 
     # every rank generates the same seeded layer and keeps its heads, so any N times the same layer
     q, k, v = device_inputs(w, 0, w.hk, dev, seed=w.config_index * 1000 + 1)
@@ -471,17 +477,19 @@ def main():
         if w.varlen:
             _ops.prefill_varlen(q, k, v, out, cu, maxlen, w.alpha, 128, 2, 4, 2, workspace=ws)
         else:
-            _ops.prefill_dense(q[None], k[None], v[None], out[None], 128, 2, 4, w.alpha, 2, 0, workspace=ws)
+            _ops.prefill_dense(q[None], k[None], v[None], out[None], 128, 2, 4, w.alpha, 2, 0, workspace=ws,
+                               q_blocks=(qb0, qb1) if rows2d else None)
 
     for _ in range(max(3, a.warmup)):
         api_step()
-        step()
+        if not rows2d:
+            step()
     torch.cuda.synchronize()
     fp.check_device_error(ws)
     # the count rows past the layout's real tiles (varlen reserves an upper bound) are unused
     cnt = ws[L["cnt"]:L["cnt"] + 4 * hq_l * L["tiles"]].view(torch.int32).view(hq_l, L["tiles"])
     real_tiles = sum(math.ceil(x / 128) for x in w.seqlens)
-    E_local = int(cnt[:, :real_tiles].sum().item())
+    E_local = int((cnt[:, qb0:qb1] if rows2d else cnt[:, :real_tiles]).sum().item())
 
     # ---- timed region (device-resident inputs): the public entry point, one call per step
     evh = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(2)) for _ in range(a.steps)]
@@ -500,16 +508,20 @@ def main():
         dist.barrier()
     clocks = clk.summary()
     t_step = sum(e0.elapsed_time(e2) for e0, e2 in evh) / a.steps
-    # ---- breakdown (not the headline): search and attention entry points, an event between
-    evs = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(a.steps)]
-    torch.cuda.synchronize()
-    for e0, e1, e2 in evs:
-        e0.record(stream)
-        step(e1)
-        e2.record(stream)
-    torch.cuda.synchronize()
-    t_search = sum(e0.elapsed_time(e1) for e0, e1, e2 in evs) / a.steps
-    t_attn = sum(e1.elapsed_time(e2) for e0, e1, e2 in evs) / a.steps
+    # ---- breakdown (not the headline): search and attention entry points, an event between.
+    # A 2-D split rank has no separate range-restricted stage entries: its whole step stands in.
+    if rows2d:
+        t_search, t_attn = t_step, t_step
+    else:
+        evs = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(a.steps)]
+        torch.cuda.synchronize()
+        for e0, e1, e2 in evs:
+            e0.record(stream)
+            step(e1)
+            e2.record(stream)
+        torch.cuda.synchronize()
+        t_search = sum(e0.elapsed_time(e1) for e0, e1, e2 in evs) / a.steps
+        t_attn = sum(e1.elapsed_time(e2) for e0, e1, e2 in evs) / a.steps
     stats = torch.tensor([t_step, t_search, t_attn, E_local], dtype=torch.float64, device=dev)
     mx, tot = stats.clone(), stats.clone()
     if world > 1:
@@ -610,7 +622,7 @@ def main():
     #          over NVLink (fpb_prefill_dense_peers, peers mapped by CUDA IPC), then a
     #          one-element all-reduce orders the ranks (a stream-ordered cross-GPU barrier).
     gather = None
-    if world > 1 and not a.no_gather:
+    if world > 1 and not a.no_gather and not rows2d:
         stage = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=dev)
         full = torch.empty((T, world * hq_l, w.d), dtype=out.dtype, device=dev)
 
@@ -695,7 +707,8 @@ def main():
     roof = {"bound": "tensor", "achieved": round(ach, 2), "peak": tflops, "unit": "TFLOP/s",
             "frac": round(ach / tflops, 4), "traffic": traffic.get("sparse_attn_kernel"),
             "kernel": "sparse_attn_kernel", "ms": round(t_a, 4),
-            "algorithmic": f"E*4*128*128*128 FLOP, E={E_local} executed block pairs on this rank",
+            "algorithmic": f"E*4*128*128*128 FLOP, E={E_local} executed block pairs on this rank"
+                           + (" (2-D split rank: time of the whole step, search included)" if rows2d else ""),
             "peak_kind": f"{peak_kind} burst bf16 (of measured)" if peak_kind == "measured" else "fallback"}
     sach = sb / (t_s * 1e-3) / 1e9
     roof_s = {"bound": "hbm", "achieved": round(sach, 1), "peak": hbm, "unit": "GB/s", "frac": round(sach / hbm, 4),
@@ -718,7 +731,8 @@ def main():
             "data": "synthetic (BASELINE generator recipe, device RNG)",
             "config": {"workload": w.name, "seq_len": sum(w.seqlens), "seqlens": w.seqlens, "q_heads": w.hq,
                        "kv_heads": w.hk, "head_dim": w.d, "alpha": w.alpha, "sink": 2, "window": 4, "last_n": 2,
-                       "parallelism": f"kv-head groups x{world}", "l2": "inputs larger than L2 (no flush)"},
+                       "parallelism": (f"kv-head groups x{w.hk} x query-block ranges x{world // w.hk}" if rows2d
+                                       else f"kv-head groups x{world}"), "l2": "inputs larger than L2 (no flush)"},
             "search_ms": round(t_s, 4), "attention_ms": round(t_a, 4),
             "executed_pairs": E_total, "density": round(E_total / P_pairs, 5),
             "roofline": roof, "roofline_search": roof_s, "e2e": e2e, "cpu_baseline": cpu,

@@ -133,11 +133,13 @@ def _dense_args(q, k, v, out):
 
 
 def prefill_dense(q, k, v, out, block_size, attention_sink, window_size, alpha, last_n_block_full, min_budget,
-                  workspace: torch.Tensor | None = None, out_peers=None):
+                  workspace: torch.Tensor | None = None, out_peers=None, q_blocks=None):
     """Full operator on (B,S,H,D) tensors; writes ``out`` in place.  Returns the workspace.
 
     ``out_peers``: device addresses (ints) of the same output slice in other GPUs' copies of
-    the output; every output tile is written there too (fpb_prefill_dense_peers)."""
+    the output; every output tile is written there too (fpb_prefill_dense_peers).
+    ``q_blocks``: (begin, end) query-block range; only those rows are searched and written,
+    with the selection rules of the whole sequence (fpb_prefill_dense_rows)."""
     lib = _lib.load()
     q, k, v, B, S, Hq, Hk, D = _dense_args(q, k, v, out)
     code = _dtype_code(q)
@@ -150,9 +152,13 @@ def prefill_dense(q, k, v, out, block_size, attention_sink, window_size, alpha, 
         args = (_P(q), _P(k), _P(v), _P(tgt), code, B, S, Hq, Hk, D, _strides(q, 3), _strides(k, 3), _strides(v, 3),
                 _strides(tgt, 3), int(block_size), int(attention_sink), int(window_size), float(alpha),
                 int(last_n_block_full), int(min_budget), _MEAN_WARPS, _P(ws), ws.numel())
+        if out_peers and q_blocks is not None:
+            raise ValueError("out_peers and q_blocks cannot be combined")
         if out_peers:
             peers = (ctypes.c_void_p * len(out_peers))(*[int(p) for p in out_peers])
             rc = lib.fpb_prefill_dense_peers(*args, peers, len(out_peers), _P(stream))
+        elif q_blocks is not None:
+            rc = lib.fpb_prefill_dense_rows(*args[:21], int(q_blocks[0]), int(q_blocks[1]), *args[21:], _P(stream))
         else:
             rc = lib.fpb_prefill_dense(*args, _P(stream))
     _lib.check(rc)

@@ -17,6 +17,7 @@
 
 #include "../../include/flashprefill_b200.h"
 #include "fp_attn.cu"
+#include "fp_attn2.cu"
 #include "fp_mean.cu"
 #include "fp_search.cu"
 
@@ -211,7 +212,17 @@ struct Geometry {
   int varlen, nseq, seqlen, total_tokens, max_seq_len, batch;
   int hq, hk, dtype;
   const int32_t* cu_seqlens;
+  int qb_lo = 0, qb_hi = -1;  // dense: query blocks [qb_lo, qb_hi) only (qb_hi < 0: all)
 };
+
+// Query-block rows of work (search items and attention items per head): dense covers the
+// chosen query blocks of every batch entry, varlen the layout's upper bound of blocks.
+int work_tiles(const Geometry& g, const Layout& L) {
+  if (g.varlen) return L.tiles;
+  const int nb = (g.seqlen + kBlock - 1) / kBlock;
+  const int hi = g.qb_hi < 0 ? nb : g.qb_hi;
+  return g.batch * (hi - g.qb_lo);
+}
 
 SeqProblem make_problem(const Geometry& g, const Layout& L, uint8_t* ws) {
   SeqProblem P{};
@@ -219,6 +230,8 @@ SeqProblem make_problem(const Geometry& g, const Layout& L, uint8_t* ws) {
   P.nseq = g.varlen ? g.nseq : g.batch;
   P.seqlen = g.seqlen;
   P.nb_dense = g.varlen ? 0 : (g.seqlen + kBlock - 1) / kBlock;
+  P.row_lo = g.varlen ? 0 : g.qb_lo;
+  P.nrows = g.varlen ? 0 : (g.qb_hi < 0 ? P.nb_dense : g.qb_hi) - g.qb_lo;
   P.tiles_ub = L.tiles;
   P.cap = L.cap;
   P.hq = g.hq;
@@ -278,16 +291,9 @@ int run_search(const Geometry& g, const void* q, const void* k, const int64_t qs
   A.normalize = g.varlen ? 0 : 1;
   A.idx = reinterpret_cast<int32_t*>(ws + L.idx);
   A.cnt = reinterpret_cast<int32_t*>(ws + L.cnt);
-  long long* dbg_t = nullptr;
-  const unsigned grid_dbg = (unsigned)L.tiles * (unsigned)g.hq;
-  if (std::getenv("FLASHPREFILL_B200_SEARCH_DBG")) {
-    FPB_CUDA(cudaMalloc(&dbg_t, sizeof(long long) * 6 * (grid_dbg / 16 + 1)));
-    FPB_CUDA(cudaMemsetAsync(dbg_t, 0, sizeof(long long) * 6 * (grid_dbg / 16 + 1), stream));
-  }
-  A.dbg_t = dbg_t;
-  const unsigned grid = (unsigned)L.tiles * (unsigned)g.hq;
+  const unsigned grid = (unsigned)work_tiles(g, L) * (unsigned)g.hq;
   const size_t psmem = search_p_smem_bytes(L.cap);
-  const bool persistent = L.cap <= kSearchMaxCap && psmem <= 227 * 1024 && !dbg_t &&
+  const bool persistent = L.cap <= kSearchMaxCap && psmem <= 227 * 1024 &&
                           std::getenv("FLASHPREFILL_B200_SEARCH_PER_ITEM") == nullptr;
   if (persistent) {
     A.counter = reinterpret_cast<int*>(ws + L.err + kSearchCounterOffset);
@@ -307,10 +313,12 @@ int run_search(const Geometry& g, const void* q, const void* k, const int64_t qs
                     fa.numRegs, kSearchPLaunchRegs, fa.maxThreadsPerBlock, kSearchPThreads, fa.sharedSizeBytes);
     }
     unsigned long long* sprof = nullptr;
+#if FPB_SEARCH_PROFILE  // debug build only: per-phase cycle sums (allocates and synchronises)
     if (std::getenv("FLASHPREFILL_B200_SEARCH_PROFILE")) {
       FPB_CUDA(cudaMalloc(&sprof, sizeof(unsigned long long) * kSpSlots));
       FPB_CUDA(cudaMemsetAsync(sprof, 0, sizeof(unsigned long long) * kSpSlots, stream));
     }
+#endif
     A.prof = sprof;
     if (g.dtype == FPB_BF16) {
       FPB_TRY(set_smem(block_search_persistent_kernel<__nv_bfloat16>, psmem));
@@ -335,17 +343,41 @@ int run_search(const Geometry& g, const void* q, const void* k, const int64_t qs
     block_search_kernel<__half><<<grid, kSearchThreads, smem, stream>>>(tm_q, tm_mk, A);
   }
   FPB_CUDA(cudaGetLastError());
-  if (dbg_t) {
-    const size_t nrec = grid_dbg / 16 + 1;
-    std::vector<long long> h(6 * nrec);
-    FPB_CUDA(cudaMemcpyAsync(h.data(), dbg_t, sizeof(long long) * 6 * nrec, cudaMemcpyDeviceToHost, stream));
-    FPB_CUDA(cudaStreamSynchronize(stream));
-    if (FILE* fh = std::fopen(std::getenv("FLASHPREFILL_B200_SEARCH_DBG"), "wb")) {
-      std::fwrite(h.data(), sizeof(long long), h.size(), fh);
-      std::fclose(fh);
-    }
-    cudaFree(dbg_t);
+  return FPB_OK;
+}
+
+// Head-pair attention kernel (fp_attn2.cu) over the block lists in the workspace.
+int run_attention2(const Geometry& g, const Layout& L, const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                   const AttnArgs& A1, cudaStream_t stream) {
+  Attn2Args A{};
+  A.P = A1.P;
+  A.c = A1.c;
+  A.idx = A1.idx;
+  A.cnt = A1.cnt;
+  A.counter = A1.counter;
+  const int group = g.hq / g.hk;
+  A.ppg = (group + 1) / 2;
+  A.total_items = work_tiles(g, L) * g.hk * A.ppg;
+  A.out = A1.out;
+  A.o_sb = A1.o_sb;
+  A.o_ss = A1.o_ss;
+  A.o_sh = A1.o_sh;
+  int sms = 0;
+  FPB_TRY(sm_count(&sms));
+  const unsigned grid = (unsigned)std::max(1, std::min(sms, A.total_items));
+  using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, Attn2Args);
+  const KernelFn kern = g.dtype == FPB_BF16 ? sparse_attn2_kernel<__nv_bfloat16> : sparse_attn2_kernel<__half>;
+  {
+    cudaFuncAttributes fa{};
+    FPB_CUDA(cudaFuncGetAttributes(&fa, (const void*)kern));
+    if (fa.numRegs != kA2LaunchRegs)
+      return fail(FPB_ECUDA, "head-pair attention kernel compiled with %d registers/thread, %d expected by its "
+                  "register split", fa.numRegs, kA2LaunchRegs);
   }
+  const size_t smem = attn2_smem_bytes();
+  FPB_TRY(set_smem(kern, smem));
+  kern<<<grid, kA2Threads, smem, stream>>>(tm_q, tm_k, tm_v, A);
+  FPB_CUDA(cudaGetLastError());
   return FPB_OK;
 }
 
@@ -364,7 +396,7 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
   AttnArgs A{};
   A.P = P;
   A.c = score_scale();
-  A.total_items = L.tiles * g.hq;
+  A.total_items = work_tiles(g, L) * g.hq;
   A.counter = reinterpret_cast<int*>(ws + L.err + kCounterOffset);
   FPB_CUDA(cudaMemsetAsync(A.counter, 0, sizeof(int), stream));
   A.idx = reinterpret_cast<const int32_t*>(ws + L.idx);
@@ -384,6 +416,11 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
       (int64_t)std::min(L.cap, ((g.varlen ? g.max_seq_len : g.seqlen) + kBlock - 1) / kBlock) * kSplitThrDen * 2 * (int64_t)grid <=
           listed_lower_bound * kSplitThrNum)
     A.split = 0;
+  // the head-pair kernel serves every call without a split plan or peer outputs
+  const char* which = std::getenv("FLASHPREFILL_B200_ATTN");
+  const bool v2 = which ? std::strcmp(which, "v2") == 0 : false;
+  if (v2 && !A.split && n_peers == 0)
+    return run_attention2(g, L, tm_q, tm_k, tm_v, A, stream);
   if (A.split) {
     SplitArgs S{};
     S.P = P;
@@ -635,10 +672,11 @@ int fpb_attention_varlen(const void* q, const void* k, const void* v, void* o, i
 
 // Fewest listed blocks a dense search can return: its lists hold at least the structural
 // blocks of every row (sinks, the local window, and whole rows for the last-N query blocks).
-int64_t dense_listed_lower_bound(int batch, int seqlen, int hq, int sink, int window, int last_n) {
+int64_t dense_listed_lower_bound(int batch, int seqlen, int hq, int sink, int window, int last_n, int qb_lo = 0,
+                                 int qb_hi = -1) {
   const int64_t nb = (seqlen + kBlock - 1) / kBlock;
   int64_t per_head = 0;
-  for (int64_t qb = 0; qb < nb; ++qb)
+  for (int64_t qb = qb_lo; qb < (qb_hi < 0 ? nb : qb_hi); ++qb)
     if (qb >= nb - last_n) {
       per_head += qb + 1;
     } else {  // |[0, sink) U (qb - window, qb]| within [0, qb]
@@ -665,6 +703,29 @@ int fpb_prefill_dense(const void* q, const void* k, const void* v, void* out, in
                      mean_model, ws, L, st));
   return run_attention(g, q, k, v, out, q_strides, k_strides, v_strides, o_strides, ws, L, workspace_bytes, st,
                        dense_listed_lower_bound(batch, seqlen, hq, attention_sink, window_size, last_n_block_full));
+}
+
+int fpb_prefill_dense_rows(const void* q, const void* k, const void* v, void* out, int dtype, int batch,
+                           int seqlen, int hq, int hk, int head_dim, const int64_t* q_strides,
+                           const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                           int block_size, int attention_sink, int window_size, float alpha, int last_n_block_full,
+                           int min_budget, int mean_model, int q_block_begin, int q_block_end, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  FPB_TRY(check_dense(q, k, dtype, batch, seqlen, hq, hk, head_dim, q_strides, k_strides, block_size));
+  FPB_TRY(check_dense_vo(v, out, v_strides, o_strides));
+  const int nb = (seqlen + kBlock - 1) / kBlock;
+  FPB_CHECK_ARG(0 <= q_block_begin && q_block_begin < q_block_end && q_block_end <= nb,
+                "query-block range [%d, %d) must be non-empty and within [0, %d)", q_block_begin, q_block_end, nb);
+  const Layout L = make_layout(0, batch, seqlen, 0, hq, hk);
+  FPB_TRY(check_ws(workspace, workspace_bytes, L));
+  Geometry g{0, batch, seqlen, 0, 0, batch, hq, hk, dtype, nullptr, q_block_begin, q_block_end};
+  auto* ws = static_cast<uint8_t*>(workspace);
+  auto st = static_cast<cudaStream_t>(stream);
+  FPB_TRY(run_search(g, q, k, q_strides, k_strides, attention_sink, window_size, alpha, last_n_block_full, min_budget,
+                     mean_model, ws, L, st));
+  return run_attention(g, q, k, v, out, q_strides, k_strides, v_strides, o_strides, ws, L, workspace_bytes, st,
+                       dense_listed_lower_bound(batch, seqlen, hq, attention_sink, window_size, last_n_block_full,
+                                                q_block_begin, q_block_end));
 }
 
 int fpb_prefill_dense_peers(const void* q, const void* k, const void* v, void* out, int dtype, int batch, int seqlen,

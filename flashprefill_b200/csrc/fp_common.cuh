@@ -25,6 +25,8 @@ struct SeqProblem {
   int nb_dense;       // dense: ceil(S/128)
   int tiles_ub;       // rows of the per-head list arrays (>= total blocks)
   int cap;            // capacity of one block list (>= nb of every sequence)
+  int row_lo, nrows;  // dense: the query blocks [row_lo, row_lo + nrows) of each batch entry are
+                      // searched and attended (the others are left alone); varlen: 0, unused
   int hq, hk;
   const int* cu_seqlens;  // varlen: device int32 [nseq+1]
   const int* cu_tile;     // varlen: device int32 [nseq+1], filled by the prep kernel
@@ -39,13 +41,12 @@ struct SeqInfo {
   int bcoord;     // batch coordinate (dense) or 0
 };
 
-// Work item -> (sequence, block).  Items are visited latest block first, so the most
-// expensive rows (late query blocks see the most key blocks) start first.
-__device__ __forceinline__ bool decode_item(const SeqProblem& P, int item, SeqInfo& s, int& blk) {
+// Key block -> (sequence, block), over every block of every sequence (pooled keys).
+__device__ __forceinline__ bool decode_block(const SeqProblem& P, int item, SeqInfo& s, int& blk) {
   if (!P.varlen) {
     const int b = item / P.nb_dense;
     if (b >= P.nseq) return false;
-    blk = P.nb_dense - 1 - (item - b * P.nb_dense);
+    blk = item - b * P.nb_dense;
     s.start = 0;
     s.len = P.seqlen;
     s.nb = P.nb_dense;
@@ -55,20 +56,39 @@ __device__ __forceinline__ bool decode_item(const SeqProblem& P, int item, SeqIn
   }
   const int total = __ldg(P.cu_tile + P.nseq);
   if (item >= total) return false;
-  const int x = total - 1 - item;
-  int lo = 0, hi = P.nseq;  // largest lo with cu_tile[lo] <= x (skips empty sequences)
+  int lo = 0, hi = P.nseq;  // largest lo with cu_tile[lo] <= item (skips empty sequences)
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
-    if (__ldg(P.cu_tile + mid) <= x) lo = mid; else hi = mid;
+    if (__ldg(P.cu_tile + mid) <= item) lo = mid; else hi = mid;
   }
   s.start = __ldg(P.cu_seqlens + lo);
   s.len = __ldg(P.cu_seqlens + lo + 1) - s.start;
   s.tile_base = __ldg(P.cu_tile + lo);
   s.nb = __ldg(P.cu_tile + lo + 1) - s.tile_base;
   s.bcoord = 0;
-  blk = x - s.tile_base;
+  blk = item - s.tile_base;
   // a sequence longer than max_seq_len is flagged by the prep kernel and skipped here
   return s.nb <= P.cap;
+}
+
+// Work item -> (sequence, query block).  Items are visited latest block first, so the most
+// expensive rows (late query blocks see the most key blocks) start first.  Dense problems
+// cover the query blocks [row_lo, row_lo + nrows) of every batch entry.
+__device__ __forceinline__ bool decode_item(const SeqProblem& P, int item, SeqInfo& s, int& blk) {
+  if (!P.varlen) {
+    const int b = item / P.nrows;
+    if (b >= P.nseq) return false;
+    blk = P.row_lo + P.nrows - 1 - (item - b * P.nrows);
+    s.start = 0;
+    s.len = P.seqlen;
+    s.nb = P.nb_dense;
+    s.tile_base = b * P.nb_dense;
+    s.bcoord = b;
+    return true;
+  }
+  const int total = __ldg(P.cu_tile + P.nseq);
+  if (item >= total) return false;
+  return decode_block(P, total - 1 - item, s, blk);
 }
 
 __device__ __forceinline__ void raise_error(uint32_t* err, uint32_t bits) {

@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(W * 32) block_mean_kernel(const T* __restrict_
                                                             int64_t sh, T* __restrict__ mk, SeqProblem P) {
   SeqInfo s;
   int kb;
-  if (!decode_item(P, blockIdx.x, s, kb)) return;
+  if (!decode_block(P, blockIdx.x, s, kb)) return;
   const int hk = blockIdx.y;
   const int t = threadIdx.x, w = t >> 5, l = (t >> 4) & 1, cg = t & 15;
   const int n_valid = min(kBlock, s.len - kb * kBlock);

@@ -41,7 +41,6 @@ struct SearchArgs {
   int normalize;    // dense path: divide by (sum + 1e-9)
   int32_t* idx;     // [hq][tiles_ub][cap]
   int32_t* cnt;     // [hq][tiles_ub]
-  long long* dbg_t; // optional phase timestamps of every 16th CTA (debug)
   int* counter;     // persistent kernel: work-item counter, zero at launch
   int total_items;  // persistent kernel: tiles_ub * hq
   unsigned long long* prof;  // persistent kernel: optional per-phase cycle sums (kSpSlots)
@@ -96,7 +95,6 @@ template <typename T>
 __global__ void __launch_bounds__(kSearchThreads, 1)
     block_search_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_mk,
                         const SearchArgs A) {
-  const long long t_start = clock64();
   const int hq = blockIdx.x % A.P.hq;
   SeqInfo s;
   int qb;
@@ -224,10 +222,8 @@ __global__ void __launch_bounds__(kSearchThreads, 1)
     const int vr = min(kBlock, s.len - qb * kBlock);  // valid query rows of this block
     const float c = A.c;
     bool ok = true;
-    long long t_first = 0;
     for (int t = 0; t < ntiles; ++t) {
       const int acc = t & 1;
-      if (t == 1 && et == 0) t_first = clock64();
       if (!mbar_wait_warp(acc_full + acc, (t >> 1) & 1, abort)) { ok = false; break; }
       tc_fence_after();
       const int kb = t * kBlock + lrow;
@@ -298,7 +294,6 @@ __global__ void __launch_bounds__(kSearchThreads, 1)
         p_arr[kb] = cand ? p : -1.f;
       }
     }
-    const long long t_tiles = clock64();
     // ---- normalise, threshold, compact (the failure decision is taken once for all 4 warps)
     if (!ok) *failed_flag = 1;
     named_bar_sync(1, 128);
@@ -381,10 +376,6 @@ __global__ void __launch_bounds__(kSearchThreads, 1)
       for (int kb = kb0; kb < kb1; ++kb)
         if (selected(kb)) out_idx[pre++] = kb;
       if (et == 0) *out_cnt = base;
-    }
-    if (A.dbg_t && et == 0 && (blockIdx.x & 15) == 0) {
-      long long* d = A.dbg_t + (blockIdx.x >> 4) * 6;
-      d[0] = t_start; d[1] = t_first; d[2] = t_tiles; d[3] = clock64(); d[4] = ntiles; d[5] = qb;
     }
   }
 

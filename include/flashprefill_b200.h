@@ -116,6 +116,22 @@ FPB_API int fpb_prefill_dense_peers(const void* q, const void* k, const void* v,
                                     int last_n_block_full, int min_budget, int mean_model, void* workspace,
                                     size_t workspace_bytes, void* const* out_peers, int n_peers, void* stream);
 
+/* fpb_prefill_dense restricted to the query blocks [q_block_begin, q_block_end) of every batch
+ * entry: their block lists are searched and their output rows written, with the selection
+ * rules of the whole sequence (the last-N rule still refers to the sequence's last blocks);
+ * other output rows are left untouched.  The union over a partition of [0, ceil(S/128)) of
+ * such calls equals one fpb_prefill_dense call.  It serves a 2-D split of one layer over
+ * GPUs (KV-head groups x query-block ranges, each GPU holding its heads' whole K/V) when
+ * there are more GPUs than KV heads.  The reference runs whole layers only
+ * (ops/flashprefill_native_forward.py:481-499); q/k/v/out and the workspace are as in
+ * fpb_prefill_dense. */
+FPB_API int fpb_prefill_dense_rows(const void* q, const void* k, const void* v, void* out, int dtype, int batch,
+                                   int seqlen, int hq, int hk, int head_dim, const int64_t* q_strides,
+                                   const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                                   int block_size, int attention_sink, int window_size, float alpha,
+                                   int last_n_block_full, int min_budget, int mean_model, int q_block_begin,
+                                   int q_block_end, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Search stage only (pooled keys + block lists into the workspace): replaces
  * compute_mean_vector + compute_block_score + normalize_scores + deal_output_score
  * (ops/flashprefill_native_forward.py:22-188,347-403). */

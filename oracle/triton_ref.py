@@ -43,8 +43,21 @@ def available() -> bool:
     return os.path.isfile(os.path.join(REF_DIR, "__init__.py"))
 
 
+def _static_compile():
+    """The reference wraps two torch helpers in torch.compile.  After a few input shapes
+    torch's dynamo would switch them to dynamic shapes, whose inductor build needs a host
+    C++/OpenMP toolchain this image lacks; compiling each shape statically (as the first
+    call of every shape does anyway) keeps them on the GPU code path."""
+    import torch._dynamo.config as dc
+    dc.automatic_dynamic_shapes = False
+    for name in ("recompile_limit", "cache_size_limit"):
+        if hasattr(dc, name):
+            setattr(dc, name, max(getattr(dc, name), 256))
+
+
 def load():
     """Import the staged reference package; returns (native module, varlen module)."""
+    _static_compile()
     if _PKG not in sys.modules:
         if not os.path.isfile(os.path.join(REF_DIR, "__init__.py")):
             raise RuntimeError("reference sources are not staged (run oracle/stage_ref.py)")

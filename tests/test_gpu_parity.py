@@ -230,3 +230,36 @@ def test_prefill_peers_writes_every_copy():
     for i, (f, sl) in enumerate(zip(fulls, slices)):
         assert torch.equal(sl, ref), f"copy {i} differs from the plain prefill"
         assert bool((f[:, :, :4] == 7.0).all()), f"copy {i}: heads outside the slice were written"
+
+
+def test_query_block_ranges_partition_the_layer():
+    """fpb_prefill_dense_rows over a partition of the query blocks (the 2-D split of one layer
+    over GPUs) gives the block lists of the whole-layer call for every row in its range, the
+    same outputs, and leaves the rows outside its range untouched."""
+    S, hq, hk, alpha = 20000, 4, 1, 0.05
+    q, k, v, cu = gu.make_packed([S], hq, hk, torch.bfloat16, seed0=31337)
+    qd, kd, vd = (t[None].to(DEV) for t in (q, k, v))
+    nb = (S + 127) // 128
+    full = torch.empty_like(qd)
+    ws_full = _ops.prefill_dense(qd, kd, vd, full, 128, 2, 4, alpha, 2, 0)
+    L = _ops.dense_layout(1, S, hq, hk)
+    cnt_f, idx_f, _ = _ops._views(ws_full, L, hq, hk, qd.dtype)
+    parts = torch.full_like(qd, float("nan"))
+    for lo, hi in [(0, 90), (90, 150), (150, nb)]:
+        piece = torch.full_like(qd, float("nan"))
+        ws = _ops.prefill_dense(qd, kd, vd, piece, 128, 2, 4, alpha, 2, 0, q_blocks=(lo, hi))
+        torch.cuda.synchronize()
+        assert fp.check_device_error(ws) == 0
+        cnt, idx, _ = _ops._views(ws, L, hq, hk, qd.dtype)
+        assert torch.equal(cnt[:, lo:hi], cnt_f[:, lo:hi])
+        for h in range(hq):
+            for qb in range(lo, hi):
+                c = int(cnt_f[h, qb])
+                assert torch.equal(idx[h, qb, :c], idx_f[h, qb, :c]), (h, qb)
+        r0, r1 = lo * 128, min(S, hi * 128)
+        assert torch.isnan(piece[:, :r0].float()).all() and torch.isnan(piece[:, r1:].float()).all()
+        parts[:, r0:r1] = piece[:, r0:r1]
+    d = (parts.float() - full.float()).abs()
+    assert d.max().item() <= gu.MAX_ABS and d.mean().item() <= 1e-4, (d.max().item(), d.mean().item())
+    with pytest.raises(ValueError):
+        _ops.prefill_dense(qd, kd, vd, parts, 128, 2, 4, alpha, 2, 0, q_blocks=(5, 5))
