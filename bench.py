@@ -376,13 +376,88 @@ def interpreter_baseline():
                       f"host, {d['selected_blocks']} blocks selected"}
 
 
+# --------------------------------------------------------------------------- cfg4
+def run_cfg4(a, rank, world, local):
+    """prefill of one 131072-token sequence of uniform random token ids
+    through a random-init Llama-3-8B (32 layers, bf16 weights ~ N(0, 0.02)), FlashPrefill
+    attention in every layer, tensor parallel over the ranks (one NCCL all-reduce after o_proj
+    and one after the MLP).  A step is one whole prefill (32 layers + last-token logits)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from flashprefill_b200.llama_prefill import LlamaConfig, TPLlamaPrefill, prefill_flops
+
+    if a.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference has no runnable CPU path for a "
+                              "32-layer 131072-token prefill (its Triton kernels need a GPU or the interpreter)"}))
+        return
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"),
+                                timeout=datetime.timedelta(seconds=300))
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    cfg = LlamaConfig()
+    S = 131072
+    model = TPLlamaPrefill(cfg, rank, world, device=dev, seed=4)
+    g = torch.Generator(device=dev)
+    g.manual_seed(4004)
+    tokens = torch.randint(0, cfg.vocab, (S,), device=dev, generator=g)
+    for _ in range(max(1, a.warmup)):
+        model.forward(tokens)
+    steps = max(1, a.steps)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    evs, attn_evs = [], []
+    with ClockSampler(local) as clk:
+        for _ in range(steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            logits = model.forward(tokens, events=attn_evs)
+            e1.record()
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = sum(x.elapsed_time(y) for x, y in evs) / steps
+    attn_ms = sum(x.elapsed_time(y) for x, y in attn_evs) / steps
+    t = torch.tensor([ms, attn_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    finite = bool(torch.isfinite(logits).all().item())
+    if rank == 0:
+        hbm, tflops, tfl_sus, peak_kind = load_peaks()
+        fl = prefill_flops(cfg, S)
+        line = {"metric": "llama3_8b prefill ms @128K (FlashPrefill in every layer, tensor parallel)",
+                "value": round(float(t[0]), 2), "unit": "ms/prefill", "n_gpus": world, "steps": steps,
+                "warmup": max(1, a.warmup), "ms_per_step": round(float(t[0]), 2), "higher_is_better": False,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (uniform random token ids, random-init weights N(0, 0.02))",
+                "config": {"workload": "cfg4_llama3_8b_prefill_128k", "seq_len": S, "layers": cfg.layers,
+                           "parallelism": f"tensor parallel x{world} (heads, MLP)"},
+                "attention_ms_per_prefill": round(float(t[1]), 2),
+                "attention_share": round(float(t[1] / t[0]), 4),
+                "gemm_tflops": round(fl / (float(t[0] - t[1]) * 1e-3) / 1e12 / world, 1),
+                "gemm_tflops_note": "projection/MLP GEMM FLOPs per GPU over the non-attention time",
+                "tokens_per_s": round(S / (float(t[0]) * 1e-3), 1), "logits_finite": finite,
+                "clocks": clk.summary(), "peak_bf16_tflops": tflops, "peak_kind": peak_kind}
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
 # --------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="l128k")
+    ap.add_argument("--workload", default="l128k",
+                    help="l128k (default), cfg1, cfg2, cfg3, or cfg4: end-to-end Llama-3-8B prefill of 131072 "
+                         "tokens, tensor parallel over the ranks")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -398,6 +473,8 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     shard = tuple(int(x) for x in a.shard.split("/")) if a.shard else None
+    if a.workload == "cfg4":
+        return run_cfg4(a, rank, world, local)
     w = workload(a.workload)
 
     if a.impl == "reference":

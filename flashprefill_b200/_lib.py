@@ -10,7 +10,8 @@ import os
 import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libflashprefill_b200.so")
+# FLASHPREFILL_B200_LIB selects another build of the same library (e.g. an instrumented one)
+LIB_PATH = os.environ.get("FLASHPREFILL_B200_LIB") or os.path.join(_HERE, "libflashprefill_b200.so")
 
 FPB_OK, FPB_EINVAL, FPB_ECUDA, FPB_EDEVICE = 0, 1, 2, 3
 FPB_BF16, FPB_FP16 = 0, 1

@@ -346,9 +346,11 @@ int run_search(const Geometry& g, const void* q, const void* k, const int64_t qs
   return FPB_OK;
 }
 
-// Head-pair attention kernel (fp_attn2.cu) over the block lists in the workspace.
-int run_attention2(const Geometry& g, const Layout& L, const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                   const AttnArgs& A1, cudaStream_t stream) {
+// Head-pair attention kernel (fp_attn2.cu) over the block lists in the workspace; with split,
+// the long-row plan runs first in head-pair mode.
+int run_attention2(const Geometry& g, const Layout& L, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                   const CUtensorMap& tm_v, const AttnArgs& A1, uint8_t* ws, bool split, cudaStream_t stream,
+                   void* const* out_peers, int n_peers) {
   Attn2Args A{};
   A.P = A1.P;
   A.c = A1.c;
@@ -365,8 +367,37 @@ int run_attention2(const Geometry& g, const Layout& L, const CUtensorMap& tm_q, 
   int sms = 0;
   FPB_TRY(sm_count(&sms));
   const unsigned grid = (unsigned)std::max(1, std::min(sms, A.total_items));
+  A.split = split && L.max_chunks >= 2;
+  if (A.split) {
+    SplitArgs S{};
+    S.P = A.P;
+    S.cnt = A.cnt;
+    S.total_items = A.total_items;
+    S.ppg = A.ppg;
+    S.max_chunks = L.max_chunks / 2;  // two tiles' partials per entry in the same area
+    S.pipelines = (int)grid;
+    S.entries = reinterpret_cast<SplitEntry*>(ws + L.sp_entries);
+    S.head = reinterpret_cast<int*>(ws + L.sp_head);
+    S.rowidx = reinterpret_cast<int*>(ws + L.sp_rowidx);
+    S.counters = reinterpret_cast<int*>(ws + L.sp_counters);
+    FPB_CUDA(cudaMemsetAsync(S.head, 0, kPlanHeadClear, stream));
+    split_scan_kernel<<<(unsigned)((A.total_items + kScanThreads - 1) / kScanThreads), kScanThreads, 0, stream>>>(S);
+    split_plan_kernel<<<1, kPlanThreads, 0, stream>>>(S);
+    FPB_CUDA(cudaGetLastError());
+    A.sp_entries = S.entries;
+    A.sp_head = S.head;
+    A.sp_rowidx = S.rowidx;
+    A.sp_counters = S.counters;
+    A.sp_part = reinterpret_cast<float*>(ws + L.sp_part);
+  }
+  A.n_peers = n_peers;
+  for (int i = 0; i < n_peers; ++i) A.peer_out[i] = out_peers[i];
   using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, Attn2Args);
-  const KernelFn kern = g.dtype == FPB_BF16 ? sparse_attn2_kernel<__nv_bfloat16> : sparse_attn2_kernel<__half>;
+  // the peer-writing instance only when there are peers: the plain one is the hot path
+  const KernelFn kern =
+      g.dtype == FPB_BF16
+          ? (n_peers ? sparse_attn2_kernel<__nv_bfloat16, true> : sparse_attn2_kernel<__nv_bfloat16, false>)
+          : (n_peers ? sparse_attn2_kernel<__half, true> : sparse_attn2_kernel<__half, false>);
   {
     cudaFuncAttributes fa{};
     FPB_CUDA(cudaFuncGetAttributes(&fa, (const void*)kern));
@@ -376,8 +407,53 @@ int run_attention2(const Geometry& g, const Layout& L, const CUtensorMap& tm_q, 
   }
   const size_t smem = attn2_smem_bytes();
   FPB_TRY(set_smem(kern, smem));
+#if FPB_ATTN_PROFILE
+  A.profile = std::getenv("FLASHPREFILL_B200_PROFILE") != nullptr;
+  if (A.profile) {
+    static const unsigned long long zeros[kA2ProfSlots] = {};
+    FPB_CUDA(cudaMemcpyToSymbolAsync(g_attn2_prof, zeros, sizeof(zeros), 0, cudaMemcpyHostToDevice, stream));
+  }
+  A.trace = std::getenv("FLASHPREFILL_B200_TRACE") != nullptr;
+  if (A.trace) {
+    static const unsigned int zero = 0;
+    FPB_CUDA(cudaMemcpyToSymbolAsync(g_attn2_trace_n, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, stream));
+  }
+#endif
   kern<<<grid, kA2Threads, smem, stream>>>(tm_q, tm_k, tm_v, A);
   FPB_CUDA(cudaGetLastError());
+#if FPB_ATTN_PROFILE
+  if (A.profile) {  // debug instrumentation: synchronises and prints per-phase cycle sums
+    unsigned long long h[kA2ProfSlots];
+    FPB_CUDA(cudaMemcpyFromSymbolAsync(h, g_attn2_prof, sizeof(h), 0, cudaMemcpyDeviceToHost, stream));
+    FPB_CUDA(cudaStreamSynchronize(stream));
+    static const char* names[kA2ProfSlots] = {
+        "sm_wait_s_full", "sm_tmem_ld_S", "sm_max", "sm_exp_pack_st", "sm_rescale", "sm_st_wait_arrive",
+        "sm_blocks", "sm_rescales", "sm_wait_o_full", "mma_wait_k_full", "mma_wait_p_full", "mma_wait_v_full",
+        "mma_wait_o_empty", "mma_wait_q_full", "mma_union_blocks", "cta_cycles(4 roles)", "mma_wait_item",
+        "prod_wait_k_empty", "prod_wait_v_empty", "prod_wait_q_empty", "prod_wait_item_empty", "sm_epilogue",
+        "-", "-"};
+    fprintf(stderr, "[fpb attn2 profile] grid=%u\n", grid);
+    for (int i = 0; i < kA2ProfSlots; ++i) fprintf(stderr, "[fpb attn2 profile] %-24s %llu\n", names[i], h[i]);
+  }
+  {
+    unsigned long long gu[4];
+    FPB_CUDA(cudaMemcpyFromSymbolAsync(gu, g_attn2_gaveup, sizeof(gu), 0, cudaMemcpyDeviceToHost, stream));
+    FPB_CUDA(cudaStreamSynchronize(stream));
+    if (gu[0]) fprintf(stderr, "[fpb attn2] first wait that gave up: block %llu thread %llu slot %llu\n", gu[0] - 1, gu[1], gu[2]);
+  }
+  if (A.trace) {  // debug: CTA 0's event trace, written to the file the variable names
+    unsigned int n = 0;
+    FPB_CUDA(cudaMemcpyFromSymbolAsync(&n, g_attn2_trace_n, sizeof(n), 0, cudaMemcpyDeviceToHost, stream));
+    FPB_CUDA(cudaStreamSynchronize(stream));
+    n = std::min(n, (unsigned)kA2TraceCap);
+    std::vector<unsigned long long> buf(2 * (size_t)n + 1);
+    FPB_CUDA(cudaMemcpyFromSymbol(buf.data(), g_attn2_trace, 16 * (size_t)n));
+    if (FILE* fh = std::fopen(std::getenv("FLASHPREFILL_B200_TRACE"), "wb")) {
+      std::fwrite(buf.data(), 16, n, fh);
+      std::fclose(fh);
+    }
+  }
+#endif
   return FPB_OK;
 }
 
@@ -417,10 +493,10 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
           listed_lower_bound * kSplitThrNum)
     A.split = 0;
   // the head-pair kernel serves every call without a split plan or peer outputs
+  // the head-pair kernel unless the per-head kernel is asked for (FLASHPREFILL_B200_ATTN=v1)
   const char* which = std::getenv("FLASHPREFILL_B200_ATTN");
-  const bool v2 = which ? std::strcmp(which, "v2") == 0 : false;
-  if (v2 && !A.split && n_peers == 0)
-    return run_attention2(g, L, tm_q, tm_k, tm_v, A, stream);
+  const bool v2 = which ? std::strcmp(which, "v1") != 0 : true;
+  if (v2) return run_attention2(g, L, tm_q, tm_k, tm_v, A, ws, A.split, stream, out_peers, n_peers);
   if (A.split) {
     SplitArgs S{};
     S.P = P;

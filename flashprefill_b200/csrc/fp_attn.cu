@@ -156,15 +156,16 @@ __device__ __noinline__ void split_store_partial(uint32_t t_o, float* dst) {
 // The last chunk of a split row to finish merges the partial results of all its chunks (row
 // r, columns hh*64..+64 of this thread):  O = sum_c O_c 2^(m_c - M) / sum_c l_c 2^(m_c - M).
 // Kept out of line so the kernel's register allocation is not shaped by it.
+// Consecutive chunks' partials are `stride` floats apart.
 template <typename T>
 __device__ __noinline__ void split_merge_row(const float* p0, int nchunks, int r, int hh, int vr, T* orow,
-                                             int64_t o_ss) {
+                                             int64_t o_ss, int64_t stride = kSplitPartBytes / 4) {
   float M = -INFINITY;
   for (int cix = 0; cix < nchunks; ++cix)
-    M = fmaxf(M, __ldcg(p0 + (int64_t)cix * (kSplitPartBytes / 4) + 128 * 128 + r));
+    M = fmaxf(M, __ldcg(p0 + (int64_t)cix * stride + 128 * 128 + r));
   float Lsum = 0.f;
   for (int cix = 0; cix < nchunks; ++cix) {
-    const float* pc = p0 + (int64_t)cix * (kSplitPartBytes / 4) + 128 * 128;
+    const float* pc = p0 + (int64_t)cix * stride + 128 * 128;
     Lsum += (__ldcg(pc + 128 + r) + __ldcg(pc + 256 + r)) * ex2_approx(__ldcg(pc + r) - M);
   }
   const float invL = 1.f / Lsum;
@@ -175,7 +176,7 @@ __device__ __noinline__ void split_merge_row(const float* p0, int nchunks, int r
 #pragma unroll
     for (int i = 0; i < 16; ++i) acc[i] = 0.f;
     for (int cix = 0; cix < nchunks; ++cix) {
-      const float* pc = p0 + (int64_t)cix * (kSplitPartBytes / 4);
+      const float* pc = p0 + (int64_t)cix * stride;
       const float sc = ex2_approx(__ldcg(pc + 128 * 128 + r) - M);
       const float4* src = reinterpret_cast<const float4*>(pc + r * 128 + hh * 64 + g * 16);
 #pragma unroll

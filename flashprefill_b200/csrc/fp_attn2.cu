@@ -28,6 +28,8 @@
 // Shared memory: Q_0, Q_1, K[2], V[2] (32 KB each, 128-byte swizzled) and the barriers.
 // The epilogue writes O / l from registers straight to global memory (each thread one row of
 // 256 contiguous bytes), so no staging tile holds back the next item's loads.
+#include <type_traits>
+
 #include "fp_common.cuh"
 
 namespace fpb {
@@ -40,6 +42,19 @@ struct Attn2Args {
   int* counter;          // work-item counter, zero at launch
   int total_items;       // tiles_ub * hk * ppg
   int ppg;               // head pairs per KV head: ceil(G / 2)
+  int profile;           // instrumented builds: accumulate g_attn2_prof
+  int trace;             // instrumented builds: record CTA 0's events in g_attn2_trace
+  // long rows split into chunks (fp_split.cu, head-pair items); split = 0 runs every item whole
+  int split;
+  const SplitEntry* sp_entries;
+  const int* sp_head;    // plan header: [0] chunk entries, [3] split threshold
+  const int* sp_rowidx;  // [items]: split-row index or -1 (items over the threshold)
+  int* sp_counters;      // [2 * entry + tile]: chunks finished, at the row's first entry
+  float* sp_part;        // per chunk entry and tile: O [128][128], m [128], l [2][128]
+  // other GPUs' copies of the output (same layout and strides as `out`, reached over NVLink):
+  // the epilogue writes every output row there too (kernel instance kPeers)
+  int n_peers;
+  void* peer_out[kMaxOutPeers];
   void* out;             // output base
   int64_t o_sb, o_ss, o_sh;  // output strides in elements
 };
@@ -50,68 +65,194 @@ constexpr int kA2Threads = 384;
 constexpr int kA2LaunchRegs = 168, kA2RoleRegs = 80, kA2SoftRegs = 208;
 static_assert(128 * kA2RoleRegs + 256 * kA2SoftRegs <= kA2Threads * kA2LaunchRegs, "register split");
 #ifndef FPB_A2_POLY_EVERY
-#define FPB_A2_POLY_EVERY 3
+#define FPB_A2_POLY_EVERY 1000
+#endif
+// 1: the exp passes of the two tiles' softmax warps on one SM sub-partition take turns
+#ifndef FPB_A2_TURNS
+#define FPB_A2_TURNS 0
 #endif
 constexpr int kA2PolyEvery = FPB_A2_POLY_EVERY;  // one exp2 pair in kA2PolyEvery on the FMA pipe
+// MMA issuing threads: 2 = one per tile (warps 1 and 3), each walking the union and issuing its
+// tile's S and PV; 1 = one thread for both tiles (warp 1)
+#ifndef FPB_A2_ISSUERS
+#define FPB_A2_ISSUERS 1
+#endif
+constexpr int kA2Issuers = FPB_A2_ISSUERS;
 constexpr uint32_t kA2Tile = 128 * 128 * 2;
 constexpr uint32_t kA2Half = kA2Tile / 2;
 
-__host__ __device__ constexpr size_t attn2_smem_bytes() { return (size_t)kA2Tile * 6 + 1024 + 1024; }
+// Rings: three K stages (a key tile is needed as soon as its S can be issued) and two V stages.
+// Pipeline variants, measured at 128K tokens on one B200 (attention ms): two K stages 2.80
+// (three 2.85); one producer thread for K and V 2.80 (a second one for V 3.21); Q released
+// after the item's last MMA 2.80 (after its last S 2.87); one MMA issuer 2.80 (one per tile
+// 3.17-3.58).  Every extra polling thread takes issue slots from the softmax warps.
+#ifndef FPB_A2_KSTAGES
+#define FPB_A2_KSTAGES 2
+#endif
+// 1: a second producer thread (warp 2) loads the V tiles; 0: the K producer loads both
+#ifndef FPB_A2_SPLIT_PRODUCER
+#define FPB_A2_SPLIT_PRODUCER 0
+#endif
+// 1: Q_t is released after the item's last S_t; 0: after the item's last MMA
+#ifndef FPB_A2_EARLY_QFREE
+#define FPB_A2_EARLY_QFREE 0
+#endif
+// 1: the MMA issuer's waits suspend between polls (try_wait with a time hint); 0: they spin
+#ifndef FPB_A2_MMA_SLEEP
+#define FPB_A2_MMA_SLEEP 0
+#endif
+constexpr int kA2KStages = FPB_A2_KSTAGES, kA2VStages = 2;
+#if FPB_A2_MMA_SLEEP
+#define A2_MMA_WAIT mbar_wait_sleep
+#else
+#define A2_MMA_WAIT mbar_wait
+#endif
+constexpr bool kA2SplitProducer = FPB_A2_SPLIT_PRODUCER, kA2EarlyQFree = FPB_A2_EARLY_QFREE;
+__host__ __device__ constexpr size_t attn2_smem_bytes() {
+  return (size_t)kA2Tile * (2 + kA2KStages + kA2VStages) + 1024 + 1024;
+}
+
+// Instrumentation (build flag -DFPB_ATTN_PROFILE=1, run time FLASHPREFILL_B200_PROFILE=1): cycle
+// sums per phase over all CTAs, recorded by one thread per role (kA2ProfNames in fp_api.cu).
+constexpr int kA2ProfSlots = 24;
+#if FPB_ATTN_PROFILE
+__device__ unsigned long long g_attn2_prof[kA2ProfSlots];
+#define A2_CLK() clock64()
+#define A2_ADD(slot, v) \
+  do {                  \
+    if (prof) atomicAdd(prof + (slot), (unsigned long long)(v)); \
+  } while (0)
+// the first wait of the launch that gives up: (block, thread, profile slot, clock)
+__device__ unsigned long long g_attn2_gaveup[4];
+#define A2_W(slot, call)                                                       \
+  ({                                                                           \
+    const unsigned long long t0_ = clock64();                                  \
+    const bool r_ = (call);                                                    \
+    A2_ADD(slot, clock64() - t0_);                                             \
+    if (!r_ && atomicCAS(&g_attn2_gaveup[0], 0ull, 1ull + blockIdx.x) == 0ull) { \
+      g_attn2_gaveup[1] = threadIdx.x;                                         \
+      g_attn2_gaveup[2] = (slot);                                              \
+      g_attn2_gaveup[3] = t0_;                                                 \
+    }                                                                          \
+    r_;                                                                        \
+  })
+// event trace of CTA 0 (FLASHPREFILL_B200_TRACE=<file>): (clock, kind << 32 | value) pairs
+constexpr int kA2TraceCap = 1 << 16;
+__device__ unsigned long long g_attn2_trace[2 * kA2TraceCap];
+__device__ unsigned int g_attn2_trace_n;
+#define A2_EV(kind, val)                                                                         \
+  do {                                                                                           \
+    if (trace_on) {                                                                              \
+      const unsigned long long now_ = clock64();                                                 \
+      const unsigned i_ = atomicAdd(trace_ctr, 1u); /* shared memory: short round trip */        \
+      if (i_ < kA2TraceCap) {                                                                    \
+        g_attn2_trace[2 * i_] = now_;                                                            \
+        g_attn2_trace[2 * i_ + 1] = ((unsigned long long)(kind) << 32) | (unsigned)(val);        \
+      }                                                                                          \
+    }                                                                                            \
+  } while (0)
+#else
+#define A2_CLK() 0ull
+#define A2_ADD(slot, v) ((void)0)
+#define A2_W(slot, call) (call)
+#define A2_EV(kind, val) ((void)0)
+#endif
 
 struct Item2 {
-  int valid;  // 0: no more work, 1: item, 2: nothing to do (padding tile of the grid)
+  int valid;  // 0: no more work, 1: item, 2: nothing to do (padding tile, or a row done as chunks)
   int start, len, bcoord, qb, row;
-  int h[2];     // query heads of the two tiles (h[1] = -1: single-head item)
-  int n[2];     // listed blocks per tile
-  int diag[2];  // the tile's last listed block is the diagonal block (causal mask)
-  int pad[4];
+  int h[2];      // query heads of the two tiles (h[1] = -1: single-head item)
+  int n[2];      // listed blocks per tile in this item (a chunk: its share of the list)
+  int diag[2];   // the tile's last block in this item is the diagonal block (causal mask)
+  int nfull[2];  // listed blocks per tile in the whole row
+  int chunk;     // split_code(entry, chunk, nchunks) of a chunk of a split row, or -1
+  int pad[5];
 };
+static_assert(sizeof(Item2) == 80, "item ring slot");
 
-template <typename T>
+// 16-byte store of output chunk q4 of a row to every peer copy of the output (plain stores over
+// NVLink into CUDA-IPC mappings; no TMA, no multicast).
+__device__ __forceinline__ void store_to_peers(const Attn2Args& A, int64_t byte_off, uint4 v) {
+  for (int p = 0; p < A.n_peers; ++p)
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(A.peer_out[p]) + byte_off) = v;
+}
+
+template <typename T, bool kPeers>
 __global__ void __launch_bounds__(kA2Threads, 1)
     sparse_attn2_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const Attn2Args A) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                  // [2] tiles
-  uint8_t* sK = smem + 2 * kA2Tile;    // [2] stages
-  uint8_t* sV = smem + 4 * kA2Tile;    // [2] stages
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kA2Tile);
+  uint8_t* sQ = smem;                               // [2] tiles
+  uint8_t* sK = smem + 2 * kA2Tile;                 // [kA2KStages]
+  uint8_t* sV = sK + kA2KStages * kA2Tile;          // [kA2VStages]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kA2VStages * kA2Tile);
   uint64_t* item_full = bars + 0;   // [slot]
   uint64_t* item_empty = bars + 2;  // [slot]
   uint64_t* q_full = bars + 4;      // [tile]
   uint64_t* q_empty = bars + 6;
-  uint64_t* k_full = bars + 8;      // [stage]
-  uint64_t* k_empty = bars + 10;
-  uint64_t* v_full = bars + 12;
-  uint64_t* v_empty = bars + 14;
+  uint64_t* k_full = bars + 8;      // [K stage], 4 reserved
+  uint64_t* k_empty = bars + 12;    // [K stage] (tile 0's, or the single issuer's)
+  uint64_t* v_full = bars + 27;     // [V stage]
+  uint64_t* v_empty = bars + 29;    // [V stage] (tile 0's, or the single issuer's)
+  // With one issuer per tile each tile releases stages on barriers of its own: a tile that
+  // lists few blocks runs ahead, and on a shared counting barrier its release of a later use
+  // of a stage could complete an earlier use's phase before the other tile is done with it.
+  uint64_t* k_empty1 = bars + 121;  // [K stage] tile 1's (after the profile counters)
+  uint64_t* v_empty1 = bars + 124;  // [V stage] tile 1's
   uint64_t* s_full = bars + 16;     // [tile]
   uint64_t* p_full = bars + 18;
   uint64_t* o_full = bars + 20;
   uint64_t* o_empty = bars + 22;
   uint64_t* mma_done = bars + 24;
-  Item2* ring = reinterpret_cast<Item2*>(bars + 32);          // [slot], 64 bytes each
-  volatile int* umask = reinterpret_cast<volatile int*>(ring + 2);  // [stage]: tiles | last << 2
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring + 3);
+  uint64_t* epi = bars + 25;        // [tile]: bounded sync of a tile's 128 softmax threads
+  Item2* ring = reinterpret_cast<Item2*>(bars + 32);          // [slot], 80 bytes each
+  int* umask_raw = reinterpret_cast<int*>(ring + 2);
+  volatile int* umask = umask_raw;  // [K stage]: tiles | last << 2
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(umask_raw + 4);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_chunk = reinterpret_cast<volatile int*>(tmem_slot + 2);  // [tile]
+  volatile int* pp_want = reinterpret_cast<volatile int*>(tmem_slot + 4);  // [tile][quad]
+  volatile int* pp_turn = reinterpret_cast<volatile int*>(tmem_slot + 12);  // [quad]
+  unsigned long long* prof_sm = reinterpret_cast<unsigned long long*>(bars + 96);  // [kA2ProfSlots]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // the recording thread of each role (producer, MMA issuer, row 0 of each softmax tile)
+  unsigned long long* prof =
+      (A.profile && (threadIdx.x == 0 || threadIdx.x == 32 || threadIdx.x == 128 || threadIdx.x == 256)) ? prof_sm
+                                                                                                           : nullptr;
+  (void)prof;
+  unsigned* trace_ctr = reinterpret_cast<unsigned*>(prof_sm + kA2ProfSlots);
+  (void)trace_ctr;
+  const bool trace_on = A.trace && blockIdx.x == 0 &&
+                        (threadIdx.x == 0 || threadIdx.x == 32 || threadIdx.x == 64 || threadIdx.x == 128 ||
+                         threadIdx.x == 256);
+  (void)trace_on;
+  const unsigned long long t_kernel0 = A2_CLK();
+  (void)t_kernel0;
+  if (threadIdx.x < kA2ProfSlots + 1) prof_sm[threadIdx.x] = 0;  // counters and the trace index
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(item_full + i, 1);
-      mbar_init(item_empty + i, 1 + 256);
-      mbar_init(q_full + i, 1);
-      mbar_init(q_empty + i, 1);
+    for (int i = 0; i < kA2KStages; ++i) {
       mbar_init(k_full + i, 1);
       mbar_init(k_empty + i, 1);
+      mbar_init(k_empty1 + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(item_full + i, 1);
+      mbar_init(item_empty + i, kA2Issuers + (kA2SplitProducer ? 1 : 0) + 256);  // issuer(s), V producer, softmax
+      mbar_init(q_full + i, 1);
+      mbar_init(q_empty + i, 1);
       mbar_init(v_full + i, 1);
       mbar_init(v_empty + i, 1);
+      mbar_init(v_empty1 + i, 1);
       mbar_init(s_full + i, 1);
       mbar_init(p_full + i, 128);
       mbar_init(o_full + i, 1);
       mbar_init(o_empty + i, 128);
+      mbar_init(epi + i, 128);
     }
-    mbar_init(mma_done, 1);
+    mbar_init(mma_done, kA2Issuers);
+    for (int i = 0; i < 12; ++i) pp_want[i] = 0;
     *abort = 0;
     fence_mbar_init();
   }
@@ -128,24 +269,56 @@ __global__ void __launch_bounds__(kA2Threads, 1)
 
   if (warp < 4) {
     regs_dec<kA2RoleRegs>();
+    // Union of a head pair's two ascending lists: calls visit(kb, mask) once per distinct block in
+    // ascending order (mask bit t: tile t lists it; bit 2: the item's last union block).  The
+    // K and the V producer walk the same union, so both number its blocks alike.
+    auto walk_union = [&](const int32_t* l0, int n0, const int32_t* l1, int n1, int qb, auto&& visit) -> bool {
+      int j0 = 0, j1 = 0;
+      int a0 = n0 > 0 ? __ldg(l0) : 0x7fffffff;
+      int a1 = n1 > 0 ? __ldg(l1) : 0x7fffffff;
+      while (j0 < n0 || j1 < n1) {
+        int kb = min(a0, a1);
+        int m = 0;
+        if (a0 == kb) {
+          m |= 1;
+          ++j0;
+          a0 = j0 < n0 ? __ldg(l0 + j0) : 0x7fffffff;
+        }
+        if (a1 == kb) {
+          m |= 2;
+          ++j1;
+          a1 = j1 < n1 ? __ldg(l1 + j1) : 0x7fffffff;
+        }
+        if (j0 >= n0 && j1 >= n1) m |= 4;
+        if (kb < 0 || kb > qb) {
+          raise_error(A.P.err, kErrIndexRange);
+          kb = qb;
+        }
+        if (!visit(kb, m)) return false;
+      }
+      return true;
+    };
     if (warp == 0 && lane == 0) {
-      // ------------------------------------------------------------ scheduler + producer
+      // ------------------------------------------------------------ scheduler + K producer
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_k);
-      prefetch_tmap(&tm_v);
       const uint64_t stream_once = l2_policy_evict_first();
-      uint32_t it = 0, kvseq = 0, qld[2] = {0, 0};
+      uint32_t it = 0, kseq = 0, qld[2] = {0, 0};
+      // chunks of split rows come first in the work order (they are the longest work)
+      const int n_ent = A.split ? A.sp_head[0] : 0;
+      const int split_thr = A.split ? A.sp_head[3] : 0x7fffffff;  // only rows above it can be split
       bool ok = true;
       while (ok) {
         const int slot = it & 1;
-        if (!mbar_wait_sleep(item_empty + slot, ((it >> 1) & 1) ^ 1, abort)) break;
+        if (!A2_W(20, mbar_wait_sleep(item_empty + slot, ((it >> 1) & 1) ^ 1, abort))) break;
         Item2 f{};
         const int id = atomicAdd(A.counter, 1);
         const int32_t* lst[2] = {nullptr, nullptr};
-        if (id >= A.total_items) {
+        if (id >= n_ent + A.total_items) {
           f.valid = 0;
         } else {
-          const int tile = id / npairs, pr = id - tile * npairs;
+          const SplitEntry se = id < n_ent ? A.sp_entries[id] : SplitEntry{id - n_ent, 0, 0, -1};
+          const int tile = se.item / npairs, pr = se.item - tile * npairs;
           const int hk = pr / A.ppg, ip = pr - hk * A.ppg;
           SeqInfo s;
           int qb;
@@ -160,19 +333,24 @@ __global__ void __launch_bounds__(kA2Threads, 1)
             f.row = s.tile_base + qb;
             f.h[0] = hk * group + 2 * ip;
             f.h[1] = 2 * ip + 1 < group ? f.h[0] + 1 : -1;
+            f.chunk = id < n_ent ? split_code(id, se.chunk, se.nchunks) : -1;
 #pragma unroll
             for (int t = 0; t < 2; ++t) {
-              f.n[t] = 0;
-              f.diag[t] = 0;
+              f.n[t] = f.nfull[t] = f.diag[t] = 0;
               if (f.h[t] < 0) continue;
               const int64_t row = (int64_t)f.h[t] * A.P.tiles_ub + f.row;
-              f.n[t] = max(0, min(__ldg(A.cnt + row), qb + 1));
-              lst[t] = A.idx + row * A.P.cap;
+              f.nfull[t] = max(0, min(__ldg(A.cnt + row), qb + 1));
+              const int j0 = id < n_ent ? se.chunk * kSplitChunk : 0;
+              f.n[t] = id < n_ent ? max(0, min(kSplitChunk, f.nfull[t] - j0)) : f.nfull[t];
+              lst[t] = A.idx + row * A.P.cap + j0;
               if (f.n[t] > 0) {
                 const int last = __ldg(lst[t] + f.n[t] - 1);
                 f.diag[t] = last == qb || last < 0 || last > qb;
               }
             }
+            // a whole row that the plan cut into chunks is done by its chunk items
+            if (id >= n_ent && max(f.nfull[0], f.nfull[1]) > split_thr && __ldg(A.sp_rowidx + se.item) >= 0)
+              f.valid = 2;
           }
         }
         ring[slot] = f;
@@ -185,126 +363,158 @@ __global__ void __launch_bounds__(kA2Threads, 1)
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (f.n[t] == 0) continue;
-          if (!mbar_wait_sleep(q_empty + t, (qld[t] & 1) ^ 1, abort)) { ok = false; break; }
+          if (!A2_W(19, mbar_wait_sleep(q_empty + t, (qld[t] & 1) ^ 1, abort))) { ok = false; break; }
           ++qld[t];
           mbar_arrive_expect_tx(q_full + t, kA2Tile);
           tma_load_4d_hint(sQ + t * kA2Tile, &tm_q, q_full + t, 0, f.h[t], qrow, f.bcoord, stream_once);
           tma_load_4d_hint(sQ + t * kA2Tile + kA2Half, &tm_q, q_full + t, 64, f.h[t], qrow, f.bcoord, stream_once);
         }
         if (!ok) break;
-        // union of the two ascending lists, one K/V tile per distinct block
-        int j0 = 0, j1 = 0;
-        int a0 = f.n[0] > 0 ? __ldg(lst[0]) : 0x7fffffff;
-        int a1 = f.n[1] > 0 ? __ldg(lst[1]) : 0x7fffffff;
-        while (j0 < f.n[0] || j1 < f.n[1]) {
-          int kb = min(a0, a1);
-          int m = 0;
-          if (a0 == kb) {
-            m |= 1;
-            ++j0;
-            a0 = j0 < f.n[0] ? __ldg(lst[0] + j0) : 0x7fffffff;
-          }
-          if (a1 == kb) {
-            m |= 2;
-            ++j1;
-            a1 = j1 < f.n[1] ? __ldg(lst[1] + j1) : 0x7fffffff;
-          }
-          if (j0 >= f.n[0] && j1 >= f.n[1]) m |= 4;  // the item's last union block
-          if (kb < 0 || kb > f.qb) {
-            raise_error(A.P.err, kErrIndexRange);
-            kb = f.qb;
-          }
-          const int krow = f.start + kb * kBlock;
-          const int st = kvseq & 1;
-          const uint32_t ph = (kvseq >> 1) & 1;
-          if (!mbar_wait_sleep(k_empty + st, ph ^ 1, abort)) { ok = false; break; }
+        ok = walk_union(lst[0], f.n[0], lst[1], f.n[1], f.qb, [&](int kb, int m) -> bool {
+          const int st = kseq % kA2KStages;
+          const uint32_t ph = (kseq / kA2KStages) & 1;
+          if (!A2_W(17, mbar_wait_sleep(k_empty + st, ph ^ 1, abort))) return false;
+          if (kA2Issuers == 2 && !A2_W(22, mbar_wait_sleep(k_empty1 + st, ph ^ 1, abort))) return false;
           umask[st] = m;
           // test hook (one-shot): the first producer to reach a key load while it is armed
           // skips that load, so the MMA issuer's wait runs out
           bool withhold = false;
-          if (kvseq == 0 && *(volatile int*)&g_test_withhold != 0) withhold = atomicExch(&g_test_withhold, 0) != 0;
+          if (kseq == 0 && *(volatile int*)&g_test_withhold != 0) withhold = atomicExch(&g_test_withhold, 0) != 0;
+          A2_EV(7, kseq);
           if (!withhold) {
+            const int krow = f.start + kb * kBlock;
             mbar_arrive_expect_tx(k_full + st, kA2Tile);
             tma_load_4d(sK + st * kA2Tile, &tm_k, k_full + st, 0, hkv, krow, f.bcoord);
             tma_load_4d(sK + st * kA2Tile + kA2Half, &tm_k, k_full + st, 64, hkv, krow, f.bcoord);
           }
-          if (!mbar_wait_sleep(v_empty + st, ph ^ 1, abort)) { ok = false; ++kvseq; break; }
-          mbar_arrive_expect_tx(v_full + st, kA2Tile);
-          tma_load_4d(sV + st * kA2Tile, &tm_v, v_full + st, 0, hkv, krow, f.bcoord);
-          tma_load_4d(sV + st * kA2Tile + kA2Half, &tm_v, v_full + st, 64, hkv, krow, f.bcoord);
-          ++kvseq;
-        }
+          if (!kA2SplitProducer) {  // this thread loads the V tile too
+            const int vs = kseq & 1;
+            const uint32_t vph = ((kseq >> 1) & 1) ^ 1;
+            if (!A2_W(18, mbar_wait_sleep(v_empty + vs, vph, abort))) return false;
+            if (kA2Issuers == 2 && !A2_W(22, mbar_wait_sleep(v_empty1 + vs, vph, abort))) return false;
+            const int vrow = f.start + kb * kBlock;
+            mbar_arrive_expect_tx(v_full + vs, kA2Tile);
+            tma_load_4d(sV + vs * kA2Tile, &tm_v, v_full + vs, 0, hkv, vrow, f.bcoord);
+            tma_load_4d(sV + vs * kA2Tile + kA2Half, &tm_v, v_full + vs, 64, hkv, vrow, f.bcoord);
+          }
+          ++kseq;
+          return true;
+        });
       }
       if (*abort) {  // let loads still in flight land before the CTA exits
         volatile int no_abort = 0;
-        for (uint32_t q = kvseq > 2 ? kvseq - 2 : 0; q < kvseq; ++q) {
-          mbar_wait(k_full + (q & 1), (q >> 1) & 1, &no_abort);
-          no_abort = 0;
-          mbar_wait(v_full + (q & 1), (q >> 1) & 1, &no_abort);
+        for (uint32_t q = kseq > kA2KStages ? kseq - kA2KStages : 0; q < kseq; ++q) {
+          mbar_wait(k_full + q % kA2KStages, (q / kA2KStages) & 1, &no_abort);
           no_abort = 0;
         }
+        if (!kA2SplitProducer)
+          for (uint32_t q = kseq > 2 ? kseq - 2 : 0; q < kseq; ++q) {
+            mbar_wait(v_full + (q & 1), (q >> 1) & 1, &no_abort);
+            no_abort = 0;
+          }
         for (int t = 0; t < 2; ++t)
           if (qld[t]) {
             mbar_wait(q_full + t, (qld[t] - 1) & 1, &no_abort);
             no_abort = 0;
           }
       }
-    } else if (warp == 1 && lane == 0) {
-      // ------------------------------------------------------------ MMA issuer
-      constexpr uint32_t id_s = idesc_f16(128, 128, DT<T>::is_bf16, false);
-      constexpr uint32_t id_o = idesc_f16(128, 128, DT<T>::is_bf16, true);
-      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
-      uint32_t it = 0, kvseq = 0, qc[2] = {0, 0}, pc[2] = {0, 0}, oc[2] = {0, 0};
-      int users[2] = {0, 0};
-      bool ok = true;
-      while (ok) {
+    } else if (kA2SplitProducer && warp == 2 && lane == 0) {
+      // ------------------------------------------------------------ V producer
+      prefetch_tmap(&tm_v);
+      uint32_t it = 0, vseq = 0;
+      while (true) {
         const int slot = it & 1;
-        if (!mbar_wait_sleep(item_full + slot, (it >> 1) & 1, abort)) break;
+        if (!A2_W(23, mbar_wait_sleep(item_full + slot, (it >> 1) & 1, abort))) break;
         const Item2 f = ring[slot];
         mbar_arrive(item_empty + slot);
         ++it;
         if (f.valid == 0) break;
         if (f.valid != 1 || (f.n[0] == 0 && f.n[1] == 0)) continue;
-        int pend[2] = {-1, -1};           // union sequence number of the block whose PV is due
-        bool first[2] = {true, true}, qw[2] = {false, false};
-        auto issue_pv = [&](int t) -> bool {
-          const int q = pend[t], st = q & 1;
-          if (first[t]) {  // the previous item's epilogue must have read O_t
-            if (!mbar_wait(o_empty + t, (oc[t] & 1) ^ 1, abort)) return false;
-            ++oc[t];
-          }
-          if (!mbar_wait(p_full + t, pc[t] & 1, abort)) return false;
-          ++pc[t];
-          if (!mbar_wait(v_full + st, (q >> 1) & 1, abort)) return false;
-          tc_fence_after();
-          const uint32_t t_s = tmem + t * 128, t_o = tmem + 256 + t * 128;
-          const uint32_t vb = v_base + st * kA2Tile;
+        const int hkv = f.h[0] / group;
+        const int j0 = f.chunk >= 0 ? ((f.chunk >> 17) & 127) * kSplitChunk : 0;
+        const int32_t* l0 = A.idx + ((int64_t)f.h[0] * A.P.tiles_ub + f.row) * A.P.cap + j0;
+        const int32_t* l1 = f.h[1] >= 0 ? A.idx + ((int64_t)f.h[1] * A.P.tiles_ub + f.row) * A.P.cap + j0 : l0;
+        if (!walk_union(l0, f.n[0], l1, f.n[1], f.qb, [&](int kb, int) -> bool {
+              const int st = vseq & 1;
+              if (!A2_W(18, mbar_wait_sleep(v_empty + st, ((vseq >> 1) & 1) ^ 1, abort))) return false;
+              if (kA2Issuers == 2 && !A2_W(22, mbar_wait_sleep(v_empty1 + st, ((vseq >> 1) & 1) ^ 1, abort))) return false;
+              A2_EV(8, vseq);
+              const int vrow = f.start + kb * kBlock;
+              mbar_arrive_expect_tx(v_full + st, kA2Tile);
+              tma_load_4d(sV + st * kA2Tile, &tm_v, v_full + st, 0, hkv, vrow, f.bcoord);
+              tma_load_4d(sV + st * kA2Tile + kA2Half, &tm_v, v_full + st, 64, hkv, vrow, f.bcoord);
+              ++vseq;
+              return true;
+            }))
+          break;
+      }
+      if (*abort) {
+        volatile int no_abort = 0;
+        for (uint32_t q = vseq > 2 ? vseq - 2 : 0; q < vseq; ++q) {
+          mbar_wait(v_full + (q & 1), (q >> 1) & 1, &no_abort);
+          no_abort = 0;
+        }
+      }
+    } else if (kA2Issuers == 2 && (warp == 1 || warp == 3) && lane == 0) {
+      // ------------------------------------------------------------ MMA issuer of one tile
+      // Each tile has its own issuing thread, so one tile's waits (its softmax, its loads)
+      // never hold back the other tile's MMAs.  Both walk every union block: a block the tile
+      // does not list still gets the tile's arrivals on the stage's empty barriers (count 2).
+      constexpr uint32_t id_s = idesc_f16(128, 128, DT<T>::is_bf16, false);
+      constexpr uint32_t id_o = idesc_f16(128, 128, DT<T>::is_bf16, true);
+      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
+      auto run = [&](auto tt) {
+        constexpr int t = decltype(tt)::value;
+        uint64_t* my_k_empty = t ? k_empty1 : k_empty;
+        uint64_t* my_v_empty = t ? v_empty1 : v_empty;
+        uint32_t it = 0, kvseq = 0, qc = 0, pc = 0, oc = 0;
+        bool ok = true;
+        while (ok) {
+          const int slot = it & 1;
+          if (!A2_W(16, mbar_wait_sleep(item_full + slot, (it >> 1) & 1, abort))) break;
+          const int valid = ring[slot].valid, n0 = ring[slot].n[0], n1 = ring[slot].n[1];
+          const int n_t = t ? n1 : n0;
+          mbar_arrive(item_empty + slot);
+          ++it;
+          if (valid == 0) break;
+          if (valid != 1 || (n0 == 0 && n1 == 0)) continue;
+          int pend = -1, s_left = n_t;
+          bool first = true, qw = false;
+          auto issue_pv = [&]() -> bool {
+            const int st = pend & 1;
+            if (first) {  // the previous item's epilogue must have read O_t
+              if (!A2_W(12, A2_MMA_WAIT(o_empty + t, (oc & 1) ^ 1, abort))) return false;
+              ++oc;
+            }
+            if (!A2_W(10, A2_MMA_WAIT(p_full + t, pc & 1, abort))) return false;
+            ++pc;
+            if (!A2_W(11, A2_MMA_WAIT(v_full + st, (pend >> 1) & 1, abort))) return false;
+            tc_fence_after();
+            const uint32_t vb = v_base + st * kA2Tile;
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks)  // A = P (TMEM, 8 packed columns per 16 keys), B = V (MN-major)
-            umma_ts(t_o, t_s + ks * 8, sdesc_sw128(vb + ks * 2048, kA2Half, 1024), id_o,
-                    (!first[t] || ks > 0) ? 1u : 0u);
-          first[t] = false;
-          if (--users[st] == 0) umma_commit(v_empty + st);
-          pend[t] = -1;
-          return true;
-        };
-        bool last = false;
-        while (!last && ok) {
-          const int st = kvseq & 1;
-          if (!mbar_wait(k_full + st, (kvseq >> 1) & 1, abort)) { ok = false; break; }
-          const int m = umask[st];
-          last = (m & 4) != 0;
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            if (pend[t] >= 0 && !issue_pv(t)) { ok = false; break; }
+            for (int ks = 0; ks < 8; ++ks)  // A = P (TMEM, 8 packed columns per 16 keys), B = V (MN-major)
+              umma_ts(tmem + 256 + t * 128, tmem + t * 128 + ks * 8, sdesc_sw128(vb + ks * 2048, kA2Half, 1024),
+                      id_o, (!first || ks > 0) ? 1u : 0u);
+            umma_commit(my_v_empty + st);
+            first = false;
+            pend = -1;
+            return true;
+          };
+          bool last = false;
+          while (!last) {
+            const int ks_ = kvseq % kA2KStages, vs = kvseq & 1;
+            if (!A2_W(9, A2_MMA_WAIT(k_full + ks_, (kvseq / kA2KStages) & 1, abort))) { ok = false; break; }
+            const int m = umask[ks_];
+            last = (m & 4) != 0;
+            if (pend >= 0 && !issue_pv()) { ok = false; break; }
             if (m & (1 << t)) {
-              if (!qw[t]) {
-                if (!mbar_wait(q_full + t, qc[t] & 1, abort)) { ok = false; break; }
-                ++qc[t];
-                qw[t] = true;
+              if (!qw) {
+                if (!A2_W(13, A2_MMA_WAIT(q_full + t, qc & 1, abort))) { ok = false; break; }
+                ++qc;
+                qw = true;
               }
               tc_fence_after();
-              const uint32_t qb_ = q_base + t * kA2Tile, kb_ = k_base + st * kA2Tile;
+              const uint32_t qb_ = q_base + t * kA2Tile, kb_ = k_base + ks_ * kA2Tile;
 #pragma unroll
               for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t off = (ks >> 2) * kA2Half + (ks & 3) * 32;
@@ -312,25 +522,136 @@ __global__ void __launch_bounds__(kA2Threads, 1)
                         ks > 0);
               }
               umma_commit(s_full + t);
-              pend[t] = (int)kvseq;
+              if (kA2EarlyQFree && --s_left == 0) umma_commit(q_empty + t);  // the item's last read of Q_t
+              pend = (int)kvseq;
+            } else {
+              // This tile does not use the block's V tile.  It still releases it, but only once
+              // the tile has landed: released earlier, a tile that skips many blocks could run
+              // a V stage's barrier two phases ahead of the producer waiting on it.
+              if (!A2_W(11, A2_MMA_WAIT(v_full + vs, (kvseq >> 1) & 1, abort))) { ok = false; break; }
+              umma_commit(my_v_empty + vs);
             }
+            umma_commit(my_k_empty + ks_);
+            ++kvseq;
           }
           if (!ok) break;
-          umma_commit(k_empty + st);
-          users[st] = __popc(m & 3);
+          if (pend >= 0 && !issue_pv()) break;
+          if (n_t > 0) {
+            umma_commit(o_full + t);
+            if (!kA2EarlyQFree) umma_commit(q_empty + t);
+          }
+        }
+      };
+      if (warp == 1) run(std::integral_constant<int, 0>{});
+      else run(std::integral_constant<int, 1>{});
+      umma_commit(mma_done);
+      volatile int no_abort = 0;
+      mbar_wait(mma_done, 0, &no_abort);
+    } else if (kA2Issuers == 1 && warp == 1 && lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      constexpr uint32_t id_s = idesc_f16(128, 128, DT<T>::is_bf16, false);
+      constexpr uint32_t id_o = idesc_f16(128, 128, DT<T>::is_bf16, true);
+      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
+      // Per-tile state is indexed only by compile-time tile numbers (generic lambdas over
+      // std::integral_constant) and per-stage counters are two scalars, so nothing of it lives
+      // in local memory.
+      uint32_t it = 0, kvseq = 0, qc[2] = {0, 0}, pc[2] = {0, 0}, oc[2] = {0, 0};
+      int users0 = 0, users1 = 0;  // PVs still to be issued on the V tile of stage 0 / 1
+      using T0 = std::integral_constant<int, 0>;
+      using T1 = std::integral_constant<int, 1>;
+      bool ok = true;
+      while (ok) {
+        const int slot = it & 1;
+        if (!A2_W(16, mbar_wait_sleep(item_full + slot, (it >> 1) & 1, abort))) break;
+        const int valid = ring[slot].valid, n0 = ring[slot].n[0], n1 = ring[slot].n[1];
+        mbar_arrive(item_empty + slot);
+        ++it;
+        if (valid == 0) break;
+        if (valid != 1 || (n0 == 0 && n1 == 0)) continue;
+        int pend[2] = {-1, -1};  // union sequence number of the block whose PV is due
+        bool first[2] = {true, true}, qw[2] = {false, false};
+        int s_left[2] = {n0, n1};  // S MMAs still to issue per tile; Q_t is free after the last
+        auto issue_pv = [&](auto tt) -> bool {
+          constexpr int t = decltype(tt)::value;
+          const int q = pend[t], st = q & 1;
+          if (first[t]) {  // the previous item's epilogue must have read O_t
+            if (!A2_W(12, A2_MMA_WAIT(o_empty + t, (oc[t] & 1) ^ 1, abort))) return false;
+            ++oc[t];
+          }
+          A2_EV(3, t);
+          if (!A2_W(10, A2_MMA_WAIT(p_full + t, pc[t] & 1, abort))) return false;
+          ++pc[t];
+          if (!A2_W(11, A2_MMA_WAIT(v_full + st, (q >> 1) & 1, abort))) return false;
+          A2_EV(11, t);
+          tc_fence_after();
+          constexpr uint32_t t_s = t * 128, t_o = 256 + t * 128;
+          const uint32_t vb = v_base + st * kA2Tile;
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)  // A = P (TMEM, 8 packed columns per 16 keys), B = V (MN-major)
+            umma_ts(tmem + t_o, tmem + t_s + ks * 8, sdesc_sw128(vb + ks * 2048, kA2Half, 1024), id_o,
+                    (!first[t] || ks > 0) ? 1u : 0u);
+          A2_EV(2, t);
+          first[t] = false;
+          if (st == 0) {
+            if (--users0 == 0) umma_commit(v_empty);
+          } else {
+            if (--users1 == 0) umma_commit(v_empty + 1);
+          }
+          pend[t] = -1;
+          return true;
+        };
+        auto issue_s = [&](auto tt, int st) -> bool {
+          constexpr int t = decltype(tt)::value;
+          if (!qw[t]) {
+            if (!A2_W(13, A2_MMA_WAIT(q_full + t, qc[t] & 1, abort))) return false;
+            ++qc[t];
+            qw[t] = true;
+          }
+          tc_fence_after();
+          A2_EV(13, t);
+          const uint32_t qb_ = q_base + t * kA2Tile, kb_ = k_base + st * kA2Tile;
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t off = (ks >> 2) * kA2Half + (ks & 3) * 32;
+            umma_ss(tmem + t * 128, sdesc_sw128(qb_ + off, 16, 1024), sdesc_sw128(kb_ + off, 16, 1024), id_s,
+                    ks > 0);
+          }
+          umma_commit(s_full + t);
+          A2_EV(1, (t << 16) | (kvseq & 0xffff));
+          // the item's last read of Q_t: the next item's Q_t may load while this one finishes
+          if (kA2EarlyQFree && --s_left[t] == 0) umma_commit(q_empty + t);
+          pend[t] = (int)kvseq;
+          return true;
+        };
+        bool last = false;
+        while (!last && ok) {
+          const int ks_ = kvseq % kA2KStages, st = kvseq & 1;  // K stage, V stage of this union block
+          A2_EV(9, kvseq);
+          if (!A2_W(9, A2_MMA_WAIT(k_full + ks_, (kvseq / kA2KStages) & 1, abort))) { ok = false; break; }
+          A2_EV(10, kvseq);
+          A2_ADD(14, 1);
+          const int m = umask[ks_];
+          last = (m & 4) != 0;
+          // tile 0: PV of its previous block, then S of this one; then the same for tile 1
+          if (pend[0] >= 0 && !issue_pv(T0{})) { ok = false; break; }
+          if ((m & 1) && !issue_s(T0{}, ks_)) { ok = false; break; }
+          if (pend[1] >= 0 && !issue_pv(T1{})) { ok = false; break; }
+          if ((m & 2) && !issue_s(T1{}, ks_)) { ok = false; break; }
+          umma_commit(k_empty + ks_);
+          if (st == 0) users0 = __popc(m & 3); else users1 = __popc(m & 3);
           ++kvseq;
         }
         if (!ok) break;
-#pragma unroll
-        for (int t = 0; t < 2; ++t)
-          if (pend[t] >= 0 && !issue_pv(t)) ok = false;
-        if (!ok) break;
-#pragma unroll
-        for (int t = 0; t < 2; ++t)
-          if (f.n[t] > 0) {
-            umma_commit(o_full + t);
-            umma_commit(q_empty + t);  // the item's last read of Q_t
-          }
+        if (pend[0] >= 0 && !issue_pv(T0{})) break;
+        if (pend[1] >= 0 && !issue_pv(T1{})) break;
+        if (n0 > 0) {
+          umma_commit(o_full);
+          if (!kA2EarlyQFree) umma_commit(q_empty);
+        }
+        if (n1 > 0) {
+          umma_commit(o_full + 1);
+          if (!kA2EarlyQFree) umma_commit(q_empty + 1);
+        }
       }
       umma_commit(mma_done);
       volatile int no_abort = 0;
@@ -346,40 +667,57 @@ __global__ void __launch_bounds__(kA2Threads, 1)
     const uint32_t t_s = tmem + t * 128 + lane_off;
     const uint32_t t_o = tmem + 256 + t * 128 + lane_off;
     const float c = A.c;
-    uint32_t it = 0, sc = 0, oc = 0;
+    uint32_t it = 0, sc = 0, oc = 0, ep = 0;
+    auto group_sync = [&]() -> bool {  // the tile's 128 softmax threads, bounded
+      mbar_arrive(epi + t);
+      return A2_W(22, mbar_wait_warp_sleep(epi + t, (ep++) & 1, abort));
+    };
     while (true) {
       const int slot = it & 1;
-      if (!mbar_wait_warp_sleep(item_full + slot, (it >> 1) & 1, abort)) break;
-      const Item2 f = ring[slot];
+      if (!A2_W(23, mbar_wait_warp_sleep(item_full + slot, (it >> 1) & 1, abort))) break;
+      // this tile's fields as scalars (a struct indexed by the runtime tile would live in local memory)
+      const Item2* fp = ring + slot;
+      const int valid = fp->valid, h_t = fp->h[t], n = fp->n[t], diag_t = fp->diag[t], nfull_t = fp->nfull[t];
+      const int start = fp->start, len = fp->len, bcoord = fp->bcoord, qbk = fp->qb, chunk = fp->chunk;
       mbar_arrive(item_empty + slot);
       ++it;
-      if (f.valid == 0) break;
-      if (f.valid != 1 || f.h[t] < 0) continue;
-      const int n = f.n[t];
-      const int vr = min(kBlock, f.len - f.qb * kBlock);
-      T* orow = reinterpret_cast<T*>(A.out) + (int64_t)f.bcoord * A.o_sb +
-                (int64_t)(f.start + f.qb * kBlock + r) * A.o_ss + (int64_t)f.h[t] * A.o_sh;
-      if (n == 0) {  // empty list: zeros (the reference's acc = 0, l = 1)
-        if (r < vr) {
+      if (valid == 0) break;
+      if (valid != 1 || h_t < 0) continue;
+      const int vr = min(kBlock, len - qbk * kBlock);
+      T* orow = reinterpret_cast<T*>(A.out) + (int64_t)bcoord * A.o_sb + (int64_t)(start + qbk * kBlock + r) * A.o_ss +
+                (int64_t)h_t * A.o_sh;
+      if (n == 0) {  // empty list: zeros (the reference's acc = 0, l = 1); a chunk item only
+                     // writes them for a row with no blocks at all, in its first chunk
+        if (r < vr && (chunk < 0 || (nfull_t == 0 && ((chunk >> 17) & 127) == 0))) {
           uint4* dst = reinterpret_cast<uint4*>(orow);
 #pragma unroll
           for (int i = 0; i < 16; ++i) dst[i] = make_uint4(0, 0, 0, 0);
+          if constexpr (kPeers) {
+            const int64_t off = reinterpret_cast<const uint8_t*>(orow) - reinterpret_cast<const uint8_t*>(A.out);
+            for (int i = 0; i < 16; ++i) store_to_peers(A, off + 16 * i, make_uint4(0, 0, 0, 0));
+          }
         }
         continue;
       }
       float m_use = -INFINITY, l = 0.f;
       bool ok = true;
       for (int j = 0; j < n; ++j) {
-        if (!mbar_wait_warp_sleep(s_full + t, sc & 1, abort)) { ok = false; break; }
+        if (!A2_W(0, mbar_wait_warp_sleep(s_full + t, sc & 1, abort))) { ok = false; break; }
         ++sc;
         tc_fence_after();
+        const unsigned long long tp0 = A2_CLK();
+        (void)tp0;
+        A2_EV(5, (t << 16) | j);
         uint32_t u[128];
         tmem_ld32(t_s, *reinterpret_cast<uint32_t(*)[32]>(u));
         tmem_ld32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(u + 32));
         tmem_ld32(t_s + 64, *reinterpret_cast<uint32_t(*)[32]>(u + 64));
         tmem_ld32(t_s + 96, *reinterpret_cast<uint32_t(*)[32]>(u + 96));
         tmem_ld_wait();
-        if (f.diag[t] && j == n - 1) {  // only the diagonal block needs the causal mask
+        const unsigned long long tp1 = A2_CLK();
+        (void)tp1;
+        A2_ADD(1, tp1 - tp0);
+        if (diag_t && j == n - 1) {  // only the diagonal block needs the causal mask
 #pragma unroll
           for (int i = 0; i < 128; ++i)
             if (i > r) u[i] = __float_as_uint(-INFINITY);
@@ -403,8 +741,25 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         }
         // P = exp2(s*c - m) as 16-bit pairs over S columns [0, 64); one pair in kA2PolyEvery
         // on the FMA pipe (exp2_poly2), the rest by ex2.approx
+        const unsigned long long tp2 = A2_CLK();
+        (void)tp2;
+        A2_ADD(2, tp2 - tp1);
         const float neg_m = -m_use;
         float rs0 = 0.f, rs1 = 0.f;
+#if FPB_A2_TURNS
+        // Turn taking (Peterson's two-party lock, one per SM sub-partition): the exp passes of
+        // this warp and of the other tile's warp on the same sub-partition alternate instead of
+        // sharing its exp2 unit.  It only orders work: after a bounded wait the pass goes ahead.
+        if (lane == 0) {
+          pp_want[t * 4 + quad] = 1;
+          pp_turn[quad] = 1 - t;
+          __threadfence_block();
+          const uint64_t tw0 = global_timer_ns();
+          while (pp_want[(1 - t) * 4 + quad] && pp_turn[quad] == 1 - t)
+            if (global_timer_ns() - tw0 > 4000) break;
+        }
+        __syncwarp();
+#endif
         // packed pair k overwrites u[k] (u[2k] and u[2k+1] are read first), so no second array
 #pragma unroll
         for (int k = 0; k < 64; ++k) {
@@ -419,31 +774,58 @@ __global__ void __launch_bounds__(kA2Threads, 1)
           add2(rs0, rs1, rs0, rs1, p0, p1);
           u[k] = DT<T>::pack(p0, p1);
         }
+#if FPB_A2_TURNS
+        __syncwarp();
+        if (lane == 0) {
+          __threadfence_block();
+          pp_want[t * 4 + quad] = 0;
+        }
+#endif
         tmem_st32(t_s, *reinterpret_cast<uint32_t(*)[32]>(u));
         tmem_st32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(u + 32));
+        const unsigned long long tp3 = A2_CLK();
+        (void)tp3;
+        A2_ADD(3, tp3 - tp2);
+        A2_ADD(6, 1);
         if (__any_sync(0xffffffffu, scale_o != 1.f)) {
+          A2_ADD(7, 1);
           // O_t holds the blocks before this one (PV_t(previous) completed before S_t(this)
-          // did); rescale this row before PV_t(this) may start (p_full below)
+          // did); rescale this row before PV_t(this) may start (p_full below).  u[64..127]
+          // are free (their S values are packed into u[0..63], which the P stores still read).
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) {
-            uint32_t o[32];
-            tmem_ld32(t_o + ch * 32, o);
+          for (int hh = 0; hh < 2; ++hh) {
+            tmem_ld32(t_o + hh * 64, *reinterpret_cast<uint32_t(*)[32]>(u + 64));
+            tmem_ld32(t_o + hh * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(u + 96));
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * scale_o);
-            tmem_st32(t_o + ch * 32, o);
+            for (int i = 64; i < 128; i += 2) {
+              float a0, a1;
+              fma2(a0, a1, __uint_as_float(u[i]), __uint_as_float(u[i + 1]), scale_o, scale_o, 0.f, 0.f);
+              u[i] = __float_as_uint(a0);
+              u[i + 1] = __float_as_uint(a1);
+            }
+            tmem_st32(t_o + hh * 64, *reinterpret_cast<uint32_t(*)[32]>(u + 64));
+            tmem_st32(t_o + hh * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(u + 96));
+            if (hh == 0) tmem_st_wait();  // the second half reloads into the same registers
           }
         }
+        const unsigned long long tp4 = A2_CLK();
+        (void)tp4;
+        A2_ADD(4, tp4 - tp3);
         tmem_st_wait();
         l += rs0 + rs1;
         tc_fence_before();
         mbar_arrive(p_full + t);
+        A2_EV(6, (t << 16) | j);
+        A2_ADD(5, A2_CLK() - tp4);
       }
       if (!ok) break;
       // ---- epilogue: O / l straight from TMEM to this thread's output row
-      if (!mbar_wait_warp_sleep(o_full + t, oc & 1, abort)) break;
+      if (!A2_W(8, mbar_wait_warp_sleep(o_full + t, oc & 1, abort))) break;
       ++oc;
       tc_fence_after();
+      const unsigned long long te0 = A2_CLK();
+      (void)te0;
       uint32_t o[128];
       tmem_ld32(t_o, *reinterpret_cast<uint32_t(*)[32]>(o));
       tmem_ld32(t_o + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
@@ -452,6 +834,40 @@ __global__ void __launch_bounds__(kA2Threads, 1)
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(o_empty + t);  // O_t may be overwritten by the next item's first PV
+      if (chunk >= 0) {  // a chunk of a split row: store the partial, the row's last chunk merges
+        const int code = chunk;
+        const int entry = code & (kSplitMaxEntries - 1), cix = (code >> 17) & 127;
+        const int e0 = entry - cix, nch = (nfull_t + kSplitChunk - 1) / kSplitChunk;
+        constexpr int64_t kStride = 2 * (kSplitPartBytes / 4);  // floats between a tile's chunk partials
+        float* part = A.sp_part + (int64_t)entry * kStride + t * (kSplitPartBytes / 4);
+        float4* po = reinterpret_cast<float4*>(part + r * 128);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          po[i] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]), __uint_as_float(o[4 * i + 2]),
+                              __uint_as_float(o[4 * i + 3]));
+        part[128 * 128 + r] = m_use;
+        part[128 * 128 + 128 + r] = l;
+        part[128 * 128 + 256 + r] = 0.f;
+        __threadfence();
+        if (!group_sync()) break;
+        if (r == 0) last_chunk[t] = atomicAdd(A.sp_counters + 2 * e0 + t, 1) == nch - 1;
+        if (!group_sync()) break;
+        if (last_chunk[t]) {
+          __threadfence();
+          T* oblk = orow - (int64_t)r * A.o_ss;
+          const float* p0 = A.sp_part + (int64_t)e0 * kStride + t * (kSplitPartBytes / 4);
+          split_merge_row<T>(p0, nch, r, 0, vr, oblk, A.o_ss, kStride);
+          split_merge_row<T>(p0, nch, r, 1, vr, oblk, A.o_ss, kStride);
+          if constexpr (kPeers) {
+            if (r < vr) {  // this thread wrote its merged row: send it on
+              const int64_t off = reinterpret_cast<const uint8_t*>(orow) - reinterpret_cast<const uint8_t*>(A.out);
+              for (int i = 0; i < 16; ++i) store_to_peers(A, off + 16 * i, reinterpret_cast<const uint4*>(orow)[i]);
+            }
+          }
+        }
+        A2_ADD(21, A2_CLK() - te0);
+        continue;
+      }
       const float inv = 1.f / l;
       if (r < vr) {
         const uint64_t pol = l2_policy_evict_first();  // the output is not read again here
@@ -463,17 +879,27 @@ __global__ void __launch_bounds__(kA2Threads, 1)
           for (int i = 0; i < 4; ++i)
             pk[i] = DT<T>::pack(__uint_as_float(o[q4 * 8 + 2 * i]) * inv, __uint_as_float(o[q4 * 8 + 2 * i + 1]) * inv);
           st_global_hint(dst + q4, make_uint4(pk[0], pk[1], pk[2], pk[3]), pol);
+          if constexpr (kPeers)
+            store_to_peers(A, reinterpret_cast<const uint8_t*>(dst + q4) - reinterpret_cast<const uint8_t*>(A.out),
+                           make_uint4(pk[0], pk[1], pk[2], pk[3]));
         }
       }
+      A2_ADD(21, A2_CLK() - te0);
     }
   }
 
+  A2_ADD(15, A2_CLK() - t_kernel0);
   tc_fence_before();
   __syncthreads();
+#if FPB_ATTN_PROFILE
+  if (A.profile && threadIdx.x < kA2ProfSlots) atomicAdd(&g_attn2_prof[threadIdx.x], prof_sm[threadIdx.x]);
+  if (A.trace && blockIdx.x == 0 && threadIdx.x == 0) g_attn2_trace_n = *trace_ctr;
+#endif
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  if constexpr (kPeers) __threadfence_system();  // peer stores ordered before what follows
   if (threadIdx.x == 0 && *abort) raise_error(A.P.err, kErrWaitTimeout);
 }
 

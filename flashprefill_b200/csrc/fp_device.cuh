@@ -91,17 +91,27 @@ __device__ __forceinline__ bool mbar_probe(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// The bounded waits below read the global timer only every kTimerEvery polls: a timer read
+// per poll, from every spinning thread, would load the SM's special-register path that the
+// softmax's exp2 instructions also use.
+#ifndef FPB_TIMER_EVERY
+#define FPB_TIMER_EVERY 32
+#endif
+constexpr uint32_t kTimerEvery = FPB_TIMER_EVERY;
+
 // Waits for the phase with the given parity to complete.  Returns false on timeout or
 // when another thread of the CTA has raised *abort (the CTA is shutting down).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_test(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns(), lim = g_wait_limit_ns;
-  while (true) {
+  for (uint32_t i = 1;; ++i) {
     if (mbar_test(bar, parity)) return true;
-    if (*abort) return false;
-    if (global_timer_ns() - t0 > lim) {
-      *abort = 1;
-      return false;
+    if (i % kTimerEvery == 0) {
+      if (*abort) return false;
+      if (global_timer_ns() - t0 > lim) {
+        *abort = 1;
+        return false;
+      }
     }
   }
 }
@@ -136,13 +146,15 @@ __device__ __forceinline__ bool mbar_wait_warp_sleep(uint64_t* bar, uint32_t par
 template <bool kProbe = false>
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort) {
   const uint64_t t0 = global_timer_ns(), lim = g_wait_limit_ns;
-  while (true) {
+  for (uint32_t i = 1;; ++i) {
     const bool done = kProbe ? mbar_probe(bar, parity) : mbar_test(bar, parity);
     if (__all_sync(0xffffffffu, done)) return true;
-    const bool stop = (*abort != 0) || (global_timer_ns() - t0 > lim);
-    if (__any_sync(0xffffffffu, stop)) {
-      *abort = 1;
-      return false;
+    if (i % kTimerEvery == 0) {
+      const bool stop = (*abort != 0) || (global_timer_ns() - t0 > lim);
+      if (__any_sync(0xffffffffu, stop)) {
+        *abort = 1;
+        return false;
+      }
     }
   }
 }

@@ -56,13 +56,15 @@ constexpr int64_t kPlanHeadBytes = kPlanCandOffset + 16 * (int64_t)kPlanMaxRows;
 struct SplitArgs {
   SeqProblem P;
   const int32_t* cnt;  // [hq][tiles_ub]
-  int total_items;     // tiles_ub * hq
+  int total_items;     // tiles_ub * hq (head items), or tiles * hk * ppg (head-pair items)
+  int ppg;             // > 0: items are head pairs (ceil(G/2) per KV head) of the head-pair kernel
   int max_chunks;
   int pipelines;       // attention pipelines (2 per CTA)
   SplitEntry* entries;
   int* head;           // plan header (above)
   int* rowidx;         // [hq][tiles_ub]: split-row index or -1, written for candidate rows only
-  int* counters;       // [max_chunks]: chunks finished, indexed by the row's first entry
+  int* counters;       // [max_chunks]: chunks finished, indexed by the row's first entry (head
+                       // pairs: two counters per entry, [2 * entry + tile])
 };
 
 // Pass 1, over all rows (one item per thread): listed blocks in total, and the rows longer
@@ -71,13 +73,26 @@ constexpr int kScanThreads = 256;
 __global__ void __launch_bounds__(kScanThreads) split_scan_kernel(const SplitArgs A) {
   const int id = blockIdx.x * kScanThreads + threadIdx.x;
   int n = 0, row = -1;
-  if (id < A.total_items) {
+  if (id < A.total_items && A.ppg == 0) {
     const int tile = id / A.P.hq, h = id - tile * A.P.hq;
     SeqInfo s;
     int qb;
     if (decode_item(A.P, tile, s, qb)) {
       row = h * A.P.tiles_ub + s.tile_base + qb;
       n = max(0, min(__ldg(A.cnt + row), qb + 1));
+    }
+  } else if (id < A.total_items) {  // a head pair: the longer of its two lists
+    const int group = A.P.hq / A.P.hk, npairs = A.P.hk * A.ppg;
+    const int tile = id / npairs, pr = id - tile * npairs;
+    const int hk = pr / A.ppg, ip = pr - hk * A.ppg;
+    SeqInfo s;
+    int qb;
+    if (decode_item(A.P, tile, s, qb)) {
+      row = id;
+      for (int t = 0; t < 2 && 2 * ip + t < group; ++t) {
+        const int h = hk * group + 2 * ip + t;
+        n = max(n, max(0, min(__ldg(A.cnt + (int64_t)h * A.P.tiles_ub + s.tile_base + qb), qb + 1)));
+      }
     }
   }
   if (n > kSplitChunk) {
@@ -150,7 +165,8 @@ __global__ void __launch_bounds__(kPlanThreads, 1) split_plan_kernel(const Split
     // entries advance for every split candidate, so those that fit are a prefix of the array
     if (c > 0 && e + c <= A.max_chunks) {
       A.rowidx[cd.y] = ci;
-      A.counters[e] = 0;
+      A.counters[A.ppg ? 2 * e : e] = 0;
+      if (A.ppg) A.counters[2 * e + 1] = 0;
       for (int k2 = 0; k2 < c; ++k2) A.entries[e + k2] = SplitEntry{cd.x, k2, c, ci};
       used_e = e + c;
       atomicAdd(&n_split, 1);
