@@ -51,13 +51,14 @@ METRIC = "sparse-prefill attn ms/layer @128K on 1/8 B200; TC util; mask exactnes
 UNIT = "ms/layer"
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of
 # each kernel on the full single-GPU workload (1 pass; the commands and figures are in
-# profiles/dram_traffic.md).  Reported as roofline traffic for those workloads on one GPU
+# profiles/dram_traffic.md and profiles/sparse_attn2_cfg1_full.md: sparse_attn2_kernel and
+# block_search_persistent_kernel).  Reported as roofline traffic for those workloads on one GPU
 # with all heads; other runs (shards, N > 1, other workloads) report null.
 NCU_TRAFFIC = {
-    "llama3_8b_layer_128k": {"sparse_attn_kernel": 2235387136 + 1032059392,
-                             "block_search_persistent_kernel": 1074923264 + 5547008},
-    "cfg1_llama3_8b_32k": {"sparse_attn_kernel": 503862272 + 227547904,
-                           "block_search_persistent_kernel": 267095552 + 3992320},
+    "llama3_8b_layer_128k": {"attention": 2119719424 + 1018989056,
+                             "search": 1074931200 + 4992000},
+    "cfg1_llama3_8b_32k": {"attention": 504239104 + 217063168,
+                           "search": 267095552 + 3992320},
 }
 
 
@@ -782,8 +783,8 @@ def main():
     t_a, t_s = float(mx[2]), float(mx[1])
     ach = af / (t_a * 1e-3) / 1e12
     roof = {"bound": "tensor", "achieved": round(ach, 2), "peak": tflops, "unit": "TFLOP/s",
-            "frac": round(ach / tflops, 4), "traffic": traffic.get("sparse_attn_kernel"),
-            "kernel": "sparse_attn_kernel", "ms": round(t_a, 4),
+            "frac": round(ach / tflops, 4), "traffic": traffic.get("attention"),
+            "kernel": "sparse_attn2_kernel", "ms": round(t_a, 4),
             "algorithmic": f"E*4*128*128*128 FLOP, E={E_local} executed block pairs on this rank"
                            + (" (2-D split rank: time of the whole step, search included)" if rows2d else ""),
             "peak_kind": f"{peak_kind} burst bf16 (of measured)" if peak_kind == "measured" else "fallback"}
@@ -791,7 +792,7 @@ def main():
     roof_s = {"bound": "hbm", "achieved": round(sach, 1), "peak": hbm, "unit": "GB/s", "frac": round(sach / hbm, 4),
               "ms": round(t_s, 4), "mma_tflops": round(sf / (t_s * 1e-3) / 1e12, 1),
               "kernels": "block_mean_kernel + block_search_kernel",
-              "traffic_search_kernel": traffic.get("block_search_persistent_kernel"),
+              "traffic_search_kernel": traffic.get("search"),
               "algorithmic": "2*(S*Hq*D + S*Hk*D) + 4*E + 4*Hq*NB bytes", "peak_kind": f"{peak_kind} HBM copy"}
     nbs = [math.ceil(L_ / 128) for L_ in w.seqlens]
     P_pairs = w.hq * sum(nb * (nb + 1) // 2 for nb in nbs)
