@@ -43,6 +43,8 @@ SIGNATURES = {
                                      _I, _I, _I, _F, _I, _I, _I, _P, _SZ, ctypes.POINTER(_P), _I, _P]),
     "fpb_prefill_dense_rows": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I64P, _I64P, _I64P, _I64P,
                                     _I, _I, _I, _F, _I, _I, _I, _I, _I, _P, _SZ, _P]),
+    "fpb_prefill_dense_chunk": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I64P, _I64P, _I64P, _I64P,
+                                     _I, _I, _I, _F, _I, _I, _I, _P, _SZ, _P]),
     "fpb_prefill_varlen": (_I, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I64P, _I64P, _I64P, _I64P,
                                 _I, _I, _I, _F, _I, _I, _P, _SZ, _P]),
     "fpb_search_dense": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _I64P, _I64P, _I, _I, _I, _F, _I, _I, _I,

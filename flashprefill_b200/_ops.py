@@ -114,13 +114,13 @@ def _views(ws, L, Hq, Hk, dtype):
 
 
 # --------------------------------------------------------------------------- dense
-def _dense_args(q, k, v, out):
+def _dense_args(q, k, v, out, allow_chunk=False):
     device = q.device
     q = _prep_input(q, "q", 4, device)
     k = _prep_input(k, "k", 4, device)
     v = _prep_input(v, "v", 4, device) if v is not None else None
     B, S, Hq, D = q.shape
-    if k.shape[0] != B or k.shape[1] != S or k.shape[3] != D:
+    if k.shape[0] != B or k.shape[3] != D or not (k.shape[1] == S or (allow_chunk and k.shape[1] > S)):
         raise ValueError(f"k shape {tuple(k.shape)} does not match q shape {tuple(q.shape)}")
     if v is not None and v.shape != k.shape:
         raise ValueError(f"v shape {tuple(v.shape)} must equal k shape {tuple(k.shape)}")
@@ -139,9 +139,17 @@ def prefill_dense(q, k, v, out, block_size, attention_sink, window_size, alpha, 
     ``out_peers``: device addresses (ints) of the same output slice in other GPUs' copies of
     the output; every output tile is written there too (fpb_prefill_dense_peers).
     ``q_blocks``: (begin, end) query-block range; only those rows are searched and written,
-    with the selection rules of the whole sequence (fpb_prefill_dense_rows)."""
+    with the selection rules of the whole sequence (fpb_prefill_dense_rows).
+    k/v longer than q: chunked prefill, the queries being the last q.shape[1] positions
+    (fpb_prefill_dense_chunk)."""
     lib = _lib.load()
-    q, k, v, B, S, Hq, Hk, D = _dense_args(q, k, v, out)
+    Skv = k.shape[1] if isinstance(k, torch.Tensor) and k.dim() == 4 else None
+    q, k, v, B, S, Hq, Hk, D = _dense_args(q, k, v, out, allow_chunk=True)
+    if Skv is not None and Skv != S:
+        if out_peers or q_blocks is not None:
+            raise ValueError("chunked prefill cannot be combined with out_peers or q_blocks")
+        return _prefill_chunk(lib, q, k, v, out, B, S, Skv, Hq, Hk, D, block_size, attention_sink, window_size,
+                              alpha, last_n_block_full, min_budget, workspace)
     code = _dtype_code(q)
     tgt = out if _tma_ok(out) else torch.empty_like(q)
     if out_peers and tgt is not out:
@@ -161,6 +169,24 @@ def prefill_dense(q, k, v, out, block_size, attention_sink, window_size, alpha, 
             rc = lib.fpb_prefill_dense_rows(*args[:21], int(q_blocks[0]), int(q_blocks[1]), *args[21:], _P(stream))
         else:
             rc = lib.fpb_prefill_dense(*args, _P(stream))
+    _lib.check(rc)
+    if tgt is not out:
+        out.copy_(tgt)
+    _finish(ws, stream)
+    return ws
+
+
+def _prefill_chunk(lib, q, k, v, out, B, Sq, Skv, Hq, Hk, D, block_size, attention_sink, window_size, alpha,
+                   last_n_block_full, min_budget, workspace):
+    code = _dtype_code(q)
+    tgt = out if _tma_ok(out) else torch.empty_like(q)
+    ws = workspace if workspace is not None else _workspace(lib.fpb_dense_workspace_bytes(B, Skv, Hq, Hk, D), q.device)
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    with torch.cuda.device(q.device):
+        rc = lib.fpb_prefill_dense_chunk(_P(q), _P(k), _P(v), _P(tgt), code, B, Sq, Skv, Hq, Hk, D, _strides(q, 3),
+                                         _strides(k, 3), _strides(v, 3), _strides(tgt, 3), int(block_size),
+                                         int(attention_sink), int(window_size), float(alpha), int(last_n_block_full),
+                                         int(min_budget), _MEAN_WARPS, _P(ws), ws.numel(), _P(stream))
     _lib.check(rc)
     if tgt is not out:
         out.copy_(tgt)

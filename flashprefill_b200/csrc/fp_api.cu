@@ -213,6 +213,7 @@ struct Geometry {
   int hq, hk, dtype;
   const int32_t* cu_seqlens;
   int qb_lo = 0, qb_hi = -1;  // dense: query blocks [qb_lo, qb_hi) only (qb_hi < 0: all)
+  int q_off = 0;              // dense chunked prefill: q/out hold key positions [q_off, seqlen)
 };
 
 // Query-block rows of work (search items and attention items per head): dense covers the
@@ -232,6 +233,7 @@ SeqProblem make_problem(const Geometry& g, const Layout& L, uint8_t* ws) {
   P.nb_dense = g.varlen ? 0 : (g.seqlen + kBlock - 1) / kBlock;
   P.row_lo = g.varlen ? 0 : g.qb_lo;
   P.nrows = g.varlen ? 0 : (g.qb_hi < 0 ? P.nb_dense : g.qb_hi) - g.qb_lo;
+  P.q_off = g.varlen ? 0 : g.q_off;
   P.tiles_ub = L.tiles;
   P.cap = L.cap;
   P.hq = g.hq;
@@ -277,7 +279,7 @@ int run_search(const Geometry& g, const void* q, const void* k, const int64_t qs
     FPB_CUDA(cudaGetLastError());
   }
   CUtensorMap tm_q, tm_mk;
-  FPB_TRY(make_map(&tm_q, q, g.dtype, g.hq, rows, batch, qs[2], qs[1], qs[0], "q"));
+  FPB_TRY(make_map(&tm_q, q, g.dtype, g.hq, rows - g.q_off, batch, qs[2], qs[1], qs[0], "q"));
   FPB_TRY(make_map(&tm_mk, ws + L.mk, g.dtype, g.hk, L.tiles, 1, kHeadDim, (int64_t)g.hk * kHeadDim, 0, "pooled k"));
   SearchArgs A{};
   A.P = P;
@@ -465,10 +467,10 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
   const int rows = g.varlen ? g.total_tokens : g.seqlen;
   const int batch = g.varlen ? 1 : g.batch;
   CUtensorMap tm_q, tm_k, tm_v, tm_o;
-  FPB_TRY(make_map(&tm_q, q, g.dtype, g.hq, rows, batch, qs[2], qs[1], qs[0], "q"));
+  FPB_TRY(make_map(&tm_q, q, g.dtype, g.hq, rows - g.q_off, batch, qs[2], qs[1], qs[0], "q"));
   FPB_TRY(make_map(&tm_k, k, g.dtype, g.hk, rows, batch, ks[2], ks[1], ks[0], "k"));
   FPB_TRY(make_map(&tm_v, v, g.dtype, g.hk, rows, batch, vs[2], vs[1], vs[0], "v"));
-  FPB_TRY(make_map(&tm_o, o, g.dtype, g.hq, rows, batch, os[2], os[1], os[0], "out"));
+  FPB_TRY(make_map(&tm_o, o, g.dtype, g.hq, rows - g.q_off, batch, os[2], os[1], os[0], "out"));
   AttnArgs A{};
   A.P = P;
   A.c = score_scale();
@@ -497,6 +499,7 @@ int run_attention(const Geometry& g, const void* q, const void* k, const void* v
   const char* which = std::getenv("FLASHPREFILL_B200_ATTN");
   const bool v2 = which ? std::strcmp(which, "v1") != 0 : true;
   if (v2) return run_attention2(g, L, tm_q, tm_k, tm_v, A, ws, A.split, stream, out_peers, n_peers);
+  FPB_CHECK_ARG(g.q_off == 0, "chunked prefill needs the head-pair attention kernel (unset FLASHPREFILL_B200_ATTN)");
   if (A.split) {
     SplitArgs S{};
     S.P = P;
@@ -802,6 +805,28 @@ int fpb_prefill_dense_rows(const void* q, const void* k, const void* v, void* ou
   return run_attention(g, q, k, v, out, q_strides, k_strides, v_strides, o_strides, ws, L, workspace_bytes, st,
                        dense_listed_lower_bound(batch, seqlen, hq, attention_sink, window_size, last_n_block_full,
                                                 q_block_begin, q_block_end));
+}
+
+int fpb_prefill_dense_chunk(const void* q, const void* k, const void* v, void* out, int dtype, int batch, int q_len,
+                            int kv_len, int hq, int hk, int head_dim, const int64_t* q_strides,
+                            const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                            int block_size, int attention_sink, int window_size, float alpha, int last_n_block_full,
+                            int min_budget, int mean_model, void* workspace, size_t workspace_bytes, void* stream) {
+  FPB_TRY(check_dense(q, k, dtype, batch, kv_len, hq, hk, head_dim, q_strides, k_strides, block_size));
+  FPB_TRY(check_dense_vo(v, out, v_strides, o_strides));
+  FPB_CHECK_ARG(q_len >= 1 && q_len <= kv_len, "q_len (%d) must be in [1, kv_len = %d]", q_len, kv_len);
+  const Layout L = make_layout(0, batch, kv_len, 0, hq, hk);
+  FPB_TRY(check_ws(workspace, workspace_bytes, L));
+  const int q_off = kv_len - q_len;
+  const int nb = (kv_len + kBlock - 1) / kBlock;
+  Geometry g{0, batch, kv_len, 0, 0, batch, hq, hk, dtype, nullptr, q_off / kBlock, nb, q_off};
+  auto* ws = static_cast<uint8_t*>(workspace);
+  auto st = static_cast<cudaStream_t>(stream);
+  FPB_TRY(run_search(g, q, k, q_strides, k_strides, attention_sink, window_size, alpha, last_n_block_full, min_budget,
+                     mean_model, ws, L, st));
+  return run_attention(g, q, k, v, out, q_strides, k_strides, v_strides, o_strides, ws, L, workspace_bytes, st,
+                       dense_listed_lower_bound(batch, kv_len, hq, attention_sink, window_size, last_n_block_full,
+                                                q_off / kBlock, nb));
 }
 
 int fpb_prefill_dense_peers(const void* q, const void* k, const void* v, void* out, int dtype, int batch, int seqlen,

@@ -359,7 +359,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         if (f.valid == 0) break;
         if (f.valid != 1 || (f.n[0] == 0 && f.n[1] == 0)) continue;
         const int hkv = f.h[0] / group;
-        const int qrow = f.start + f.qb * kBlock;
+        const int qrow = f.start + f.qb * kBlock - A.P.q_off;  // rows before a chunk load as zeros
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (f.n[t] == 0) continue;
@@ -683,12 +683,14 @@ __global__ void __launch_bounds__(kA2Threads, 1)
       ++it;
       if (valid == 0) break;
       if (valid != 1 || h_t < 0) continue;
+      // rows this thread may write: inside the sequence and (chunked prefill) at or after q_off
       const int vr = min(kBlock, len - qbk * kBlock);
-      T* orow = reinterpret_cast<T*>(A.out) + (int64_t)bcoord * A.o_sb + (int64_t)(start + qbk * kBlock + r) * A.o_ss +
-                (int64_t)h_t * A.o_sh;
+      const bool row_out = r < vr && qbk * kBlock + r >= A.P.q_off;
+      T* orow = reinterpret_cast<T*>(A.out) + (int64_t)bcoord * A.o_sb +
+                (int64_t)(start + qbk * kBlock + r - A.P.q_off) * A.o_ss + (int64_t)h_t * A.o_sh;
       if (n == 0) {  // empty list: zeros (the reference's acc = 0, l = 1); a chunk item only
                      // writes them for a row with no blocks at all, in its first chunk
-        if (r < vr && (chunk < 0 || (nfull_t == 0 && ((chunk >> 17) & 127) == 0))) {
+        if (row_out && (chunk < 0 || (nfull_t == 0 && ((chunk >> 17) & 127) == 0))) {
           uint4* dst = reinterpret_cast<uint4*>(orow);
 #pragma unroll
           for (int i = 0; i < 16; ++i) dst[i] = make_uint4(0, 0, 0, 0);
@@ -852,14 +854,14 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         if (!group_sync()) break;
         if (r == 0) last_chunk[t] = atomicAdd(A.sp_counters + 2 * e0 + t, 1) == nch - 1;
         if (!group_sync()) break;
-        if (last_chunk[t]) {
+        if (last_chunk[t] && row_out) {
           __threadfence();
           T* oblk = orow - (int64_t)r * A.o_ss;
           const float* p0 = A.sp_part + (int64_t)e0 * kStride + t * (kSplitPartBytes / 4);
           split_merge_row<T>(p0, nch, r, 0, vr, oblk, A.o_ss, kStride);
           split_merge_row<T>(p0, nch, r, 1, vr, oblk, A.o_ss, kStride);
           if constexpr (kPeers) {
-            if (r < vr) {  // this thread wrote its merged row: send it on
+            {  // this thread wrote its merged row: send it on
               const int64_t off = reinterpret_cast<const uint8_t*>(orow) - reinterpret_cast<const uint8_t*>(A.out);
               for (int i = 0; i < 16; ++i) store_to_peers(A, off + 16 * i, reinterpret_cast<const uint4*>(orow)[i]);
             }
@@ -869,7 +871,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         continue;
       }
       const float inv = 1.f / l;
-      if (r < vr) {
+      if (row_out) {
         const uint64_t pol = l2_policy_evict_first();  // the output is not read again here
         uint4* dst = reinterpret_cast<uint4*>(orow);
 #pragma unroll

@@ -27,6 +27,8 @@ struct SeqProblem {
   int cap;            // capacity of one block list (>= nb of every sequence)
   int row_lo, nrows;  // dense: the query blocks [row_lo, row_lo + nrows) of each batch entry are
                       // searched and attended (the others are left alone); varlen: 0, unused
+  int q_off;          // dense chunked prefill: key positions before the first query row (the q
+                      // and out tensors hold positions [q_off, seqlen)); 0 otherwise
   int hq, hk;
   const int* cu_seqlens;  // varlen: device int32 [nseq+1]
   const int* cu_tile;     // varlen: device int32 [nseq+1], filled by the prep kernel

@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(kSearchThreads, 1)
     if (lane == 0) {
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_mk);
-      const int qrow = s.start + qb * kBlock;
+      const int qrow = s.start + qb * kBlock - A.P.q_off;  // may be negative: rows before the chunk load as zeros
       mbar_arrive_expect_tx(q_full, kTileBytes);
       tma_load_4d(sQ, &tm_q, q_full, 0, hq, qrow, s.bcoord);
       tma_load_4d(sQ + kHalfTile, &tm_q, q_full, 64, hq, qrow, s.bcoord);
@@ -558,7 +558,7 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
         const int qs = qn & 1;
         if (!SP_TW(kSpProdQ, mbar_wait_sleep(q_empty + qs, ((qn >> 1) & 1) ^ 1, abort))) break;
         ++qn;
-        const int qrow = f.start + f.qb * kBlock;
+        const int qrow = f.start + f.qb * kBlock - A.P.q_off;  // rows before a chunk load as zeros
         mbar_arrive_expect_tx(q_full + qs, kTileBytes);
         tma_load_4d(sQ + qs * kTileBytes, &tm_q, q_full + qs, 0, f.h, qrow, f.bcoord);
         tma_load_4d(sQ + qs * kTileBytes + kHalfTile, &tm_q, q_full + qs, 64, f.h, qrow, f.bcoord);

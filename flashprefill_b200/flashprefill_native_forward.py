@@ -31,7 +31,9 @@ def flash_prefill(
 
     block_size must be 128 (the reference asserts block_size == k_stride and uses it for
     both; its model code always passes 128).  The softmax scale is 1/sqrt(head_dim), as in
-    the reference.  Raises ValueError/TypeError for unsupported shapes or dtypes and
+    the reference.  k/v may be longer than q (chunked prefill over a cached prefix): the
+    queries are then the last q.shape[1] positions of the k/v sequence, selected with the
+    whole sequence's block structure (the reference sends that case to dense attention).  Raises ValueError/TypeError for unsupported shapes or dtypes and
     flashprefill_b200.FlashPrefillError for CUDA failures.
     """
     _ops.prefill_dense(q, k, v, out, block_size, attention_sink, window_size, alpha, last_n_block_full,

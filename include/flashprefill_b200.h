@@ -132,6 +132,22 @@ FPB_API int fpb_prefill_dense_rows(const void* q, const void* k, const void* v, 
                                    int last_n_block_full, int min_budget, int mean_model, int q_block_begin,
                                    int q_block_end, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Chunked (prefix) prefill: the queries are the last q_len positions of a kv_len-token sequence
+ * (q and out (B, q_len, Hq, D); k and v (B, kv_len, Hk, D), the cached prefix followed by the
+ * chunk).  Block structure, pooled keys and the selection rules are those of the whole
+ * kv_len-token sequence (the last-N rule refers to its last blocks); a query block that starts
+ * before the chunk scores its missing rows as zero rows, as the search scores the padded rows of
+ * a partial last block.  The workspace is that of fpb_prefill_dense for kv_len tokens.  With
+ * q_len = kv_len it equals fpb_prefill_dense.  No counterpart in the reference, which sends
+ * chunked prefills to dense attention (patches/patch_loader_vllm_0_10_0.py:272-300,
+ * ruler/models/llama.py:310-333). */
+FPB_API int fpb_prefill_dense_chunk(const void* q, const void* k, const void* v, void* out, int dtype, int batch,
+                                    int q_len, int kv_len, int hq, int hk, int head_dim, const int64_t* q_strides,
+                                    const int64_t* k_strides, const int64_t* v_strides,
+                                    const int64_t* o_strides, int block_size, int attention_sink,
+                                    int window_size, float alpha, int last_n_block_full, int min_budget,
+                                    int mean_model, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Search stage only (pooled keys + block lists into the workspace): replaces
  * compute_mean_vector + compute_block_score + normalize_scores + deal_output_score
  * (ops/flashprefill_native_forward.py:22-188,347-403). */

@@ -263,3 +263,45 @@ def test_query_block_ranges_partition_the_layer():
     assert d.max().item() <= gu.MAX_ABS and d.mean().item() <= 1e-4, (d.max().item(), d.mean().item())
     with pytest.raises(ValueError):
         _ops.prefill_dense(qd, kd, vd, parts, 128, 2, 4, alpha, 2, 0, q_blocks=(5, 5))
+
+
+@pytest.mark.parametrize("kv_len,q_len", [(3000, 1000), (4096, 1024), (1000, 1000), (2200, 37)])
+def test_chunked_prefill_matches_oracle(kv_len, q_len):
+    """Chunked prefill: queries are the last q_len positions of a kv_len-token sequence.  The
+    oracle runs the whole sequence with the query rows before the chunk set to zero (the
+    operator's definition: missing rows score as zero rows); block lists of the chunk's query
+    blocks must match it and the chunk's outputs must match the fp32 recomputation."""
+    hq, hk, alpha = 4, 1, 0.1
+    q, k, v, cu = gu.make_packed([kv_len], hq, hk, torch.bfloat16, seed0=kv_len + q_len)
+    q_off = kv_len - q_len
+    qz = q.clone()
+    qz[:q_off] = 0
+    res = _oracle(qz, k, cu, hq, hk, torch.bfloat16, alpha, 2, 4, 2, True)
+    qd = q[q_off:][None].to(DEV)
+    kd, vd = k[None].to(DEV), v[None].to(DEV)
+    out = torch.full_like(qd, float("nan"))
+    ws = _ops.prefill_dense(qd, kd, vd, out, 128, 2, 4, alpha, 2, 0)
+    torch.cuda.synchronize()
+    assert fp.check_device_error(ws) == 0
+    L = _ops.dense_layout(1, kv_len, hq, hk)
+    cnt, idx, _ = _ops._views(ws, L, hq, hk, torch.bfloat16)
+    nb = (kv_len + 127) // 128
+    qb0 = q_off // 128
+    sel = res["sel"][0]
+    near = res["near"][0]
+    got = np.zeros_like(sel)
+    cnt_h, idx_h = cnt.cpu().numpy(), idx.cpu().numpy()
+    for h in range(hq):
+        for qb in range(qb0, nb):
+            got[h, qb, idx_h[h, qb, :cnt_h[h, qb]]] = True
+    diff = (got ^ sel)[:, qb0:]
+    assert int((diff & ~near[:, qb0:]).sum()) == 0
+    ref = gu.ref_attention_rows(qz, k, v, cu, [got], hq, hk)
+    e = np.abs(out[0].float().cpu().numpy() - ref[q_off:])
+    print(f"chunk kv={kv_len} q={q_len}: max-abs {e.max():.3e} mean-abs {e.mean():.3e}")
+    assert e.max() <= gu.MAX_ABS and e.mean() <= gu.MEAN_ABS
+    if q_off % 128 == 0:  # whole query blocks: the same rows of the full prefill, bit for bit
+        full = torch.empty_like(kd.expand(-1, -1, hq, -1).contiguous())
+        fp.flash_prefill(q[None].to(DEV), kd, vd, full, 128, 2, 4, alpha, 2, 0)
+        torch.cuda.synchronize()
+        assert torch.equal(full[:, q_off:], out)
