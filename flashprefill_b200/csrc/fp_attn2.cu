@@ -252,7 +252,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
       mbar_init(epi + i, 128);
     }
     mbar_init(mma_done, kA2Issuers);
-    for (int i = 0; i < 12; ++i) pp_want[i] = 0;
+    for (int i = 0; i < 12; ++i) pp_want[i] = 0;  // want flags, then the turn and two exit counters
     *abort = 0;
     fence_mbar_init();
   }
@@ -748,16 +748,29 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         A2_ADD(2, tp2 - tp1);
         const float neg_m = -m_use;
         float rs0 = 0.f, rs1 = 0.f;
-#if FPB_A2_TURNS
-        // Turn taking (Peterson's two-party lock, one per SM sub-partition): the exp passes of
-        // this warp and of the other tile's warp on the same sub-partition alternate instead of
-        // sharing its exp2 unit.  It only orders work: after a bounded wait the pass goes ahead.
+#if FPB_A2_TURNS == 1
+        // Turn taking per SM sub-partition (Peterson's two-party lock): the exp passes of this
+        // warp and of the other tile's warp on the same sub-partition alternate.
         if (lane == 0) {
           pp_want[t * 4 + quad] = 1;
           pp_turn[quad] = 1 - t;
           __threadfence_block();
           const uint64_t tw0 = global_timer_ns();
           while (pp_want[(1 - t) * 4 + quad] && pp_turn[quad] == 1 - t)
+            if (global_timer_ns() - tw0 > 4000) break;
+        }
+        __syncwarp();
+#elif FPB_A2_TURNS == 2
+        // Turn taking per tile: a warp starts its exp pass when no warp of the other tile wants
+        // one, or when it is this tile's turn; the last of this tile's four warps to finish hands
+        // the turn over.  All four warps of a tile follow one order, so the tiles' exp passes
+        // alternate as wholes.  It only orders work: after a bounded wait the pass goes ahead.
+        if (lane == 0) {
+          pp_want[t * 4 + quad] = 1;
+          __threadfence_block();
+          const uint64_t tw0 = global_timer_ns();
+          while (pp_turn[0] != t && (pp_want[(1 - t) * 4] | pp_want[(1 - t) * 4 + 1] | pp_want[(1 - t) * 4 + 2] |
+                                     pp_want[(1 - t) * 4 + 3]))
             if (global_timer_ns() - tw0 > 4000) break;
         }
         __syncwarp();
@@ -776,11 +789,18 @@ __global__ void __launch_bounds__(kA2Threads, 1)
           add2(rs0, rs1, rs0, rs1, p0, p1);
           u[k] = DT<T>::pack(p0, p1);
         }
-#if FPB_A2_TURNS
+#if FPB_A2_TURNS == 1
         __syncwarp();
         if (lane == 0) {
           __threadfence_block();
           pp_want[t * 4 + quad] = 0;
+        }
+#elif FPB_A2_TURNS == 2
+        __syncwarp();
+        if (lane == 0) {
+          __threadfence_block();
+          pp_want[t * 4 + quad] = 0;
+          if (atomicAdd(const_cast<int*>(pp_turn) + 1 + t, 1) % 4 == 3) pp_turn[0] = 1 - t;  // last of 4 warps
         }
 #endif
         tmem_st32(t_s, *reinterpret_cast<uint32_t(*)[32]>(u));

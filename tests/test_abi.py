@@ -139,3 +139,26 @@ def test_install_as_ops_aliases_reference_import_paths():
                 sys.modules.pop(k, None)
             else:
                 sys.modules[k] = v
+
+
+def test_chunk_and_range_entries_reject_bad_sizes_on_the_host(lib):
+    """fpb_prefill_dense_chunk (q_len must be in [1, kv_len]) and fpb_prefill_dense_rows (the
+    query-block range must be non-empty and inside the sequence) refuse before any CUDA call;
+    the timeout test hook refuses limits outside [1 ms, 1 s]; the tile-count bounds refuse
+    problems whose lists would overflow the workspace indexing."""
+    P = ctypes.c_void_p
+    st = _lib.i64arr([1024 * 4 * 128, 4 * 128, 128])
+    sk = _lib.i64arr([1024 * 2 * 128, 2 * 128, 128])
+    for q_len, kv_len in [(0, 1024), (2048, 1024)]:
+        rc = lib.fpb_prefill_dense_chunk(P(256), P(512), P(768), P(1024), 0, 1, q_len, kv_len, 4, 2, 128, st, sk, sk,
+                                         st, 128, 2, 4, 0.1, 2, 0, 4, P(4096), 1 << 30, None)
+        assert rc == _lib.FPB_EINVAL and "q_len" in lib.fpb_last_error().decode()
+    for b, e in [(3, 3), (-1, 2), (0, 9)]:
+        rc = lib.fpb_prefill_dense_rows(P(256), P(512), P(768), P(1024), 0, 1, 1024, 4, 2, 128, st, sk, sk, st, 128,
+                                        2, 4, 0.1, 2, 0, 4, b, e, P(4096), 1 << 30, None)
+        assert rc == _lib.FPB_EINVAL and "query-block range" in lib.fpb_last_error().decode()
+    assert lib.fpb_test_set_fault(0, 10) == _lib.FPB_EINVAL
+    assert lib.fpb_test_set_fault(0, 5_000_000_000) == _lib.FPB_EINVAL
+    rc = lib.fpb_prefill_dense(P(256), P(512), P(768), P(1024), 0, 1 << 20, 1 << 20, 4, 2, 128, st, sk, sk, st,
+                               128, 2, 4, 0.1, 2, 0, 4, P(4096), 1 << 30, None)
+    assert rc == _lib.FPB_EINVAL and "too large" in lib.fpb_last_error().decode()
