@@ -97,6 +97,16 @@ constexpr uint32_t kA2Half = kA2Tile / 2;
 #ifndef FPB_A2_EARLY_QFREE
 #define FPB_A2_EARLY_QFREE 0
 #endif
+// 1: the producer prefetches an item's Q tiles into L2 as soon as it has fetched the item, before
+// it waits for the Q buffers to be free
+#ifndef FPB_A2_QPREFETCH
+#define FPB_A2_QPREFETCH 0
+#endif
+// 1: the producer issues an item's first K/V loads before it waits for the Q buffers
+#ifndef FPB_A2_KFIRST
+#define FPB_A2_KFIRST 0
+#endif
+constexpr bool kA2KFirst = FPB_A2_KFIRST;
 // 1: the MMA issuer's waits suspend between polls (try_wait with a time hint); 0: they spin
 #ifndef FPB_A2_MMA_SLEEP
 #define FPB_A2_MMA_SLEEP 0
@@ -360,16 +370,32 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         if (f.valid != 1 || (f.n[0] == 0 && f.n[1] == 0)) continue;
         const int hkv = f.h[0] / group;
         const int qrow = f.start + f.qb * kBlock - A.P.q_off;  // rows before a chunk load as zeros
+#if FPB_A2_QPREFETCH
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if (f.n[t] == 0) continue;
-          if (!A2_W(19, mbar_wait_sleep(q_empty + t, (qld[t] & 1) ^ 1, abort))) { ok = false; break; }
-          ++qld[t];
-          mbar_arrive_expect_tx(q_full + t, kA2Tile);
-          tma_load_4d_hint(sQ + t * kA2Tile, &tm_q, q_full + t, 0, f.h[t], qrow, f.bcoord, stream_once);
-          tma_load_4d_hint(sQ + t * kA2Tile + kA2Half, &tm_q, q_full + t, 64, f.h[t], qrow, f.bcoord, stream_once);
-        }
-        if (!ok) break;
+        for (int t = 0; t < 2; ++t)
+          if (f.n[t] > 0) {
+            tma_prefetch_4d(&tm_q, 0, f.h[t], qrow, f.bcoord);
+            tma_prefetch_4d(&tm_q, 64, f.h[t], qrow, f.bcoord);
+          }
+#endif
+        // Q_0 and Q_1 of the item: before its first K/V tiles, or (FPB_A2_KFIRST) right after them,
+        // so that the item's first K/V loads do not queue behind the wait for the Q buffers
+        bool q_pending = true;
+        auto load_q = [&]() -> bool {
+          q_pending = false;
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            if (f.n[t] == 0) continue;
+            if (!A2_W(19, mbar_wait_sleep(q_empty + t, (qld[t] & 1) ^ 1, abort))) return false;
+            ++qld[t];
+            mbar_arrive_expect_tx(q_full + t, kA2Tile);
+            tma_load_4d_hint(sQ + t * kA2Tile, &tm_q, q_full + t, 0, f.h[t], qrow, f.bcoord, stream_once);
+            tma_load_4d_hint(sQ + t * kA2Tile + kA2Half, &tm_q, q_full + t, 64, f.h[t], qrow, f.bcoord,
+                             stream_once);
+          }
+          return true;
+        };
+        if (!kA2KFirst && !load_q()) break;
         ok = walk_union(lst[0], f.n[0], lst[1], f.n[1], f.qb, [&](int kb, int m) -> bool {
           const int st = kseq % kA2KStages;
           const uint32_t ph = (kseq / kA2KStages) & 1;
@@ -398,6 +424,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
             tma_load_4d(sV + vs * kA2Tile + kA2Half, &tm_v, v_full + vs, 64, hkv, vrow, f.bcoord);
           }
           ++kseq;
+          if (q_pending && !load_q()) return false;
           return true;
         });
       }
