@@ -107,6 +107,10 @@ constexpr uint32_t kA2Half = kA2Tile / 2;
 #define FPB_A2_KFIRST 0
 #endif
 constexpr bool kA2KFirst = FPB_A2_KFIRST;
+#ifndef FPB_A2_ORDER
+#define FPB_A2_ORDER 0
+#endif
+constexpr int kA2Order = FPB_A2_ORDER, kA2HotTiles = 8;
 // 1: the MMA issuer's waits suspend between polls (try_wait with a time hint); 0: they spin
 #ifndef FPB_A2_MMA_SLEEP
 #define FPB_A2_MMA_SLEEP 0
@@ -308,6 +312,18 @@ __global__ void __launch_bounds__(kA2Threads, 1)
       }
       return true;
     };
+    // Visit order of whole items (position -> item id = tile * npairs + pair).  Default: heavy
+    // tiles first, all pairs of a tile together.  FPB_A2_ORDER=1: the kA2HotTiles heaviest tiles
+    // first as before, then KV head by KV head, so that the items in flight share one KV head's
+    // K/V and its re-reads hit L2.
+    auto visit_order = [&](int pos) -> int {
+      if (kA2Order == 0) return pos;
+      const int ntiles = A.total_items / npairs, hot = min(kA2HotTiles, ntiles);
+      if (pos < hot * npairs) return pos;
+      const int r = pos - hot * npairs, rest = ntiles - hot;
+      const int hk = r / (rest * A.ppg), w = r - hk * rest * A.ppg;
+      return (hot + w / A.ppg) * npairs + hk * A.ppg + w % A.ppg;
+    };
     if (warp == 0 && lane == 0) {
       // ------------------------------------------------------------ scheduler + K producer
       prefetch_tmap(&tm_q);
@@ -327,7 +343,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         if (id >= n_ent + A.total_items) {
           f.valid = 0;
         } else {
-          const SplitEntry se = id < n_ent ? A.sp_entries[id] : SplitEntry{id - n_ent, 0, 0, -1};
+          const SplitEntry se = id < n_ent ? A.sp_entries[id] : SplitEntry{visit_order(id - n_ent), 0, 0, -1};
           const int tile = se.item / npairs, pr = se.item - tile * npairs;
           const int hk = pr / A.ppg, ip = pr - hk * A.ppg;
           SeqInfo s;
