@@ -191,6 +191,27 @@ __device__ __forceinline__ void store_to_peers(const Attn2Args& A, int64_t byte_
     *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(A.peer_out[p]) + byte_off) = v;
 }
 
+// The 32 output rows a warp has just written (lane l: row pointer `row`, written iff `valid`)
+// sent on to every peer copy of the output.  Each lane wrote a whole 256-byte row; read back
+// (visible to the warp after __syncwarp), the rows go out with consecutive lanes on consecutive
+// 16-byte pieces of a row, so the NVLink writes are full 256-byte segments.  Whole warp only.
+template <typename T>
+__device__ __forceinline__ void warp_rows_to_peers(const Attn2Args& A, const T* row, bool valid) {
+  __syncwarp();
+  const unsigned vmask = __ballot_sync(0xffffffffu, valid);
+  const int lane = threadIdx.x & 31;
+  const long long mine = reinterpret_cast<long long>(row);
+#pragma unroll 4
+  for (int i = 0; i < 16; ++i) {
+    const int c = i * 32 + lane, rl = c >> 4, piece = c & 15;
+    const long long src = __shfl_sync(0xffffffffu, mine, rl);
+    if ((vmask >> rl) & 1u) {
+      const uint4* p = reinterpret_cast<const uint4*>(src) + piece;
+      store_to_peers(A, reinterpret_cast<const uint8_t*>(p) - reinterpret_cast<const uint8_t*>(A.out), *p);
+    }
+  }
+}
+
 template <typename T, bool kPeers>
 __global__ void __launch_bounds__(kA2Threads, 1)
     sparse_attn2_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -733,15 +754,13 @@ __global__ void __launch_bounds__(kA2Threads, 1)
                 (int64_t)(start + qbk * kBlock + r - A.P.q_off) * A.o_ss + (int64_t)h_t * A.o_sh;
       if (n == 0) {  // empty list: zeros (the reference's acc = 0, l = 1); a chunk item only
                      // writes them for a row with no blocks at all, in its first chunk
-        if (row_out && (chunk < 0 || (nfull_t == 0 && ((chunk >> 17) & 127) == 0))) {
+        const bool zero_row = row_out && (chunk < 0 || (nfull_t == 0 && ((chunk >> 17) & 127) == 0));
+        if (zero_row) {
           uint4* dst = reinterpret_cast<uint4*>(orow);
 #pragma unroll
           for (int i = 0; i < 16; ++i) dst[i] = make_uint4(0, 0, 0, 0);
-          if constexpr (kPeers) {
-            const int64_t off = reinterpret_cast<const uint8_t*>(orow) - reinterpret_cast<const uint8_t*>(A.out);
-            for (int i = 0; i < 16; ++i) store_to_peers(A, off + 16 * i, make_uint4(0, 0, 0, 0));
-          }
         }
+        if constexpr (kPeers) warp_rows_to_peers<T>(A, orow, zero_row);
         continue;
       }
       float m_use = -INFINITY, l = 0.f;
@@ -917,18 +936,15 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         if (!group_sync()) break;
         if (r == 0) last_chunk[t] = atomicAdd(A.sp_counters + 2 * e0 + t, 1) == nch - 1;
         if (!group_sync()) break;
-        if (last_chunk[t] && row_out) {
-          __threadfence();
-          T* oblk = orow - (int64_t)r * A.o_ss;
-          const float* p0 = A.sp_part + (int64_t)e0 * kStride + t * (kSplitPartBytes / 4);
-          split_merge_row<T>(p0, nch, r, 0, vr, oblk, A.o_ss, kStride);
-          split_merge_row<T>(p0, nch, r, 1, vr, oblk, A.o_ss, kStride);
-          if constexpr (kPeers) {
-            {  // this thread wrote its merged row: send it on
-              const int64_t off = reinterpret_cast<const uint8_t*>(orow) - reinterpret_cast<const uint8_t*>(A.out);
-              for (int i = 0; i < 16; ++i) store_to_peers(A, off + 16 * i, reinterpret_cast<const uint4*>(orow)[i]);
-            }
+        if (last_chunk[t]) {  // the same for every thread of the tile
+          if (row_out) {
+            __threadfence();
+            T* oblk = orow - (int64_t)r * A.o_ss;
+            const float* p0 = A.sp_part + (int64_t)e0 * kStride + t * (kSplitPartBytes / 4);
+            split_merge_row<T>(p0, nch, r, 0, vr, oblk, A.o_ss, kStride);
+            split_merge_row<T>(p0, nch, r, 1, vr, oblk, A.o_ss, kStride);
           }
+          if constexpr (kPeers) warp_rows_to_peers<T>(A, orow, row_out);  // the merged rows, sent on
         }
         A2_ADD(21, A2_CLK() - te0);
         continue;
@@ -944,11 +960,9 @@ __global__ void __launch_bounds__(kA2Threads, 1)
           for (int i = 0; i < 4; ++i)
             pk[i] = DT<T>::pack(__uint_as_float(o[q4 * 8 + 2 * i]) * inv, __uint_as_float(o[q4 * 8 + 2 * i + 1]) * inv);
           st_global_hint(dst + q4, make_uint4(pk[0], pk[1], pk[2], pk[3]), pol);
-          if constexpr (kPeers)
-            store_to_peers(A, reinterpret_cast<const uint8_t*>(dst + q4) - reinterpret_cast<const uint8_t*>(A.out),
-                           make_uint4(pk[0], pk[1], pk[2], pk[3]));
         }
       }
+      if constexpr (kPeers) warp_rows_to_peers<T>(A, orow, row_out);
       A2_ADD(21, A2_CLK() - te0);
     }
   }

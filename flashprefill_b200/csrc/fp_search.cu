@@ -410,6 +410,12 @@ constexpr int kSearchPThreads = 640;
 constexpr int kSearchPLaunchRegs = 96, kSearchPRoleRegs = 64, kSearchPEpiRegs = 144;
 static_assert(384 * kSearchPRoleRegs + 256 * kSearchPEpiRegs <= kSearchPThreads * kSearchPLaunchRegs, "split");
 constexpr int kSearchRing = 4;
+// 1: one exp2 pair in four of the persistent search's exp pass on the FMA pipe; 0: all on MUFU
+// (measured at 128K: 0.807 ms with all on MUFU, 0.813 with the quarter on the FMA pipe)
+#ifndef FPB_SEARCH_POLY
+#define FPB_SEARCH_POLY 0
+#endif
+constexpr bool kSearchPoly = FPB_SEARCH_POLY;
 constexpr int kSearchMaxCap = 2048;
 constexpr int kSearchStages = 4;  // pooled-key tiles in flight and TMEM accumulators (2 per epilogue group)
 
@@ -724,7 +730,7 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
                 for (int i = 0; i < 64; i += 2) {
                   float x0, x1, e0, e1;
                   fma2(x0, x1, FPB_S(i), FPB_S(i + 1), c, c, nm, nm);
-                  if (((i >> 1) & 3) == 3) {
+                  if (kSearchPoly && ((i >> 1) & 3) == 3) {
                     exp2_poly2(x0, x1, e0, e1);
                   } else {
                     e0 = ex2_approx(x0);
