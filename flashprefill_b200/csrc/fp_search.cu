@@ -407,8 +407,17 @@ constexpr int kSearchPThreads = 640;
 // Register split: compiled for 96 (= 65536 / 640, rounded down to a multiple of 8); role,
 // idle and selection warps give back to 64, the epilogue warps grow to 144: per
 // sub-partition 3*64 + 2*144 = 480 = 5*96.
-constexpr int kSearchPLaunchRegs = 96, kSearchPRoleRegs = 64, kSearchPEpiRegs = 144;
-static_assert(384 * kSearchPRoleRegs + 256 * kSearchPEpiRegs <= kSearchPThreads * kSearchPLaunchRegs, "split");
+// Tile-epilogue groups (4 warps each, tiles dealt round robin) and selection groups (4 warps
+// each, items dealt round robin); the two counts add up to 4.
+#ifndef FPB_SEARCH_EPI_GROUPS
+#define FPB_SEARCH_EPI_GROUPS 2
+#endif
+constexpr int kSearchEpiGroups = FPB_SEARCH_EPI_GROUPS, kSearchSelGroups = 4 - kSearchEpiGroups;
+static_assert(kSearchEpiGroups >= 2 && kSearchEpiGroups <= 3, "epilogue groups");
+constexpr int kSearchSelWarp0 = 4 + 4 * kSearchEpiGroups;  // first selection warp
+constexpr int kSearchPLaunchRegs = 96, kSearchPRoleRegs = 64, kSearchPEpiRegs = kSearchEpiGroups == 2 ? 144 : 112;
+static_assert((128 + 128 * kSearchSelGroups) * kSearchPRoleRegs + 128 * kSearchEpiGroups * kSearchPEpiRegs <=
+                  kSearchPThreads * kSearchPLaunchRegs, "split");
 constexpr int kSearchRing = 4;
 // 1: one exp2 pair in four of the persistent search's exp pass on the FMA pipe; 0: all on MUFU
 // (measured at 128K: 0.807 ms with all on MUFU, 0.813 with the quarter on the FMA pipe)
@@ -499,7 +508,7 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(q_full + i, 1);
       mbar_init(q_empty + i, 1);
-      mbar_init(arr_full + i, 256);
+      mbar_init(arr_full + i, 128 * kSearchEpiGroups);
       mbar_init(arr_empty + i, 128);
       mrun[i] = float_to_ordered(-INFINITY);
     }
@@ -523,7 +532,7 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const int group = A.P.hq / A.P.hk;
 
-  const bool epi_warp = warp >= 4 && warp < 12;
+  const bool epi_warp = warp >= 4 && warp < kSearchSelWarp0;
   if (warp == 0) {
     // ------------------------------------------------------------ scheduler + TMA producer
     regs_dec<kSearchPRoleRegs>();
@@ -641,7 +650,7 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
   } else if (epi_warp) {
     // ------------------------------------------------------------ tile epilogue (warps 4..11)
     regs_inc<kSearchPEpiRegs>();
-    const int eg = (warp - 4) >> 2;     // group: tiles with tc % 2 == eg
+    const int eg = (warp - 4) >> 2;     // group: tiles with tc % kSearchEpiGroups == eg
     const int quad = warp & 3;
     const int lrow = quad * 32 + lane;  // TMEM lane = key block within the tile
     const float c = A.c;
@@ -664,7 +673,7 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
         const int ntiles = qb / kBlock + 1;
         for (int j = 0; j < ntiles; ++j, ++tc) {
           const int t = tile_order(j, ntiles);
-          if ((int)(tc & 1) != eg) continue;  // the other group's tile
+          if ((int)(tc % kSearchEpiGroups) != eg) continue;  // another group's tile
           const int acc = tc % kSearchStages;
           if (!SP_TW(kSpEpiAcc, mbar_wait_warp_sleep(acc_full + acc, (tc / kSearchStages) & 1, abort))) {
             ok = false;
@@ -773,9 +782,9 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
   } else {
     // ------------------------------------------------------------ selection (warps 12..19)
     regs_dec<kSearchPRoleRegs>();
-    const int sg = (warp - 12) >> 2;          // group: array slot sg; fast items alternate too
-    const int es = threadIdx.x - 384 - sg * 128;  // 0..127
-    const int wq = (warp - 12) & 3;
+    const int sg = (warp - kSearchSelWarp0) >> 2;  // group: items dealt round robin (fast ones too)
+    const int es = threadIdx.x - 32 * kSearchSelWarp0 - sg * 128;  // 0..127
+    const int wq = (warp - kSearchSelWarp0) & 3;
     float* red = red_all + sg * 4;
     int* red_i = red_i_all + sg * 4;
     int* red_k = red_k_all + sg * 4;
@@ -792,14 +801,14 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
         int32_t* out_idx = A.idx + ((int64_t)f.h * A.P.tiles_ub + row) * cap;
         int32_t* out_cnt = A.cnt + (int64_t)f.h * A.P.tiles_ub + row;
         if (f.fast) {  // every causal block
-          if ((fn++ & 1) == (uint32_t)sg) {
+          if ((fn++ % kSearchSelGroups) == (uint32_t)sg) {
             for (int kb = es; kb <= qb; kb += 128) out_idx[kb] = kb;
             if (es == 0) *out_cnt = qb + 1;
           }
-        } else if ((an++ & 1) != (uint32_t)sg) {
-          // the other group's item
+        } else if ((an++ % kSearchSelGroups) != (uint32_t)sg) {
+          // another group's item
         } else {
-          const int a = sg;
+          const int a = (an - 1) & 1;  // the item's array slot
           if (!SP_TW(kSpSelArr, mbar_wait_warp_sleep(arr_full + a, ((an - 1) >> 1) & 1, abort))) break;
           float* m_arr = arr + a * 2 * cap;
           float* p_arr = m_arr + cap;
@@ -890,7 +899,7 @@ __global__ void __launch_bounds__(kSearchPThreads, 1)
   }
   // recording threads: producer, issuer, the first epilogue thread of group 0, the first selection thread
 #if FPB_SEARCH_PROFILE
-  if (A.prof && (threadIdx.x == 0 || threadIdx.x == 32 || threadIdx.x == 128 || threadIdx.x == 384)) {
+  if (A.prof && (threadIdx.x == 0 || threadIdx.x == 32 || threadIdx.x == 128 || threadIdx.x == 32 * kSearchSelWarp0)) {
     pacc[kSpCta] = threadIdx.x == 0 ? clock64() - t_k0 : 0;
     for (int i = 0; i < kSpSlots; ++i)
       if (pacc[i]) atomicAdd(A.prof + i, pacc[i]);
