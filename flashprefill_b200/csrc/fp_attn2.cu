@@ -107,6 +107,12 @@ constexpr uint32_t kA2Half = kA2Tile / 2;
 #define FPB_A2_KFIRST 0
 #endif
 constexpr bool kA2KFirst = FPB_A2_KFIRST;
+// > 0: the producer prefetches into L2 the K and V tiles of the list entries this far ahead of
+// the ones it loads
+#ifndef FPB_A2_AHEAD
+#define FPB_A2_AHEAD 0
+#endif
+constexpr int kA2Ahead = FPB_A2_AHEAD;
 #ifndef FPB_A2_ORDER
 #define FPB_A2_ORDER 0
 #endif
@@ -116,6 +122,25 @@ constexpr int kA2Order = FPB_A2_ORDER, kA2HotTiles = 8;
 #define FPB_A2_MMA_SLEEP 0
 #endif
 constexpr int kA2KStages = FPB_A2_KSTAGES, kA2VStages = 2;
+// Timing experiments only (wrong results): skip the exp2 pass / the O rescale
+#ifndef FPB_A2_TIMING_NOEXP
+#define FPB_A2_TIMING_NOEXP 0
+#endif
+#ifndef FPB_A2_TIMING_NOSOFTMAX
+#define FPB_A2_TIMING_NOSOFTMAX 0
+#endif
+#ifndef FPB_A2_TIMING_NORESCALE
+#define FPB_A2_TIMING_NORESCALE 0
+#endif
+// 1: the softmax warps poll for S without suspending (0: try_wait with a suspend-time hint)
+#ifndef FPB_A2_SM_SPIN
+#define FPB_A2_SM_SPIN 0
+#endif
+#if FPB_A2_SM_SPIN
+#define A2_SM_WAIT mbar_wait_warp<false>
+#else
+#define A2_SM_WAIT mbar_wait_warp_sleep
+#endif
 #if FPB_A2_MMA_SLEEP
 #define A2_MMA_WAIT mbar_wait_sleep
 #else
@@ -307,10 +332,15 @@ __global__ void __launch_bounds__(kA2Threads, 1)
     // Union of a head pair's two ascending lists: calls visit(kb, mask) once per distinct block in
     // ascending order (mask bit t: tile t lists it; bit 2: the item's last union block).  The
     // K and the V producer walk the same union, so both number its blocks alike.
-    auto walk_union = [&](const int32_t* l0, int n0, const int32_t* l1, int n1, int qb, auto&& visit) -> bool {
+    auto walk_union = [&](const int32_t* l0, int n0, const int32_t* l1, int n1, int qb, auto&& visit,
+                          auto&& ahead) -> bool {
       int j0 = 0, j1 = 0;
       int a0 = n0 > 0 ? __ldg(l0) : 0x7fffffff;
       int a1 = n1 > 0 ? __ldg(l1) : 0x7fffffff;
+      if (kA2Ahead > 0) {  // the first entries' tiles, then one entry per advance, kA2Ahead ahead
+        for (int j = 1; j < kA2Ahead && j < n0; ++j) ahead(__ldg(l0 + j));
+        for (int j = 1; j < kA2Ahead && j < n1; ++j) ahead(__ldg(l1 + j));
+      }
       while (j0 < n0 || j1 < n1) {
         int kb = min(a0, a1);
         int m = 0;
@@ -318,11 +348,13 @@ __global__ void __launch_bounds__(kA2Threads, 1)
           m |= 1;
           ++j0;
           a0 = j0 < n0 ? __ldg(l0 + j0) : 0x7fffffff;
+          if (kA2Ahead > 0 && j0 + kA2Ahead - 1 < n0) ahead(__ldg(l0 + j0 + kA2Ahead - 1));
         }
         if (a1 == kb) {
           m |= 2;
           ++j1;
           a1 = j1 < n1 ? __ldg(l1 + j1) : 0x7fffffff;
+          if (kA2Ahead > 0 && j1 + kA2Ahead - 1 < n1) ahead(__ldg(l1 + j1 + kA2Ahead - 1));
         }
         if (j0 >= n0 && j1 >= n1) m |= 4;
         if (kb < 0 || kb > qb) {
@@ -463,6 +495,13 @@ __global__ void __launch_bounds__(kA2Threads, 1)
           ++kseq;
           if (q_pending && !load_q()) return false;
           return true;
+        }, [&](int kb) {  // L2 prefetch of a block's K and V tiles, kA2Ahead list entries ahead
+          if (kb < 0 || kb > f.qb) return;
+          const int row = f.start + kb * kBlock;
+          tma_prefetch_4d(&tm_k, 0, hkv, row, f.bcoord);
+          tma_prefetch_4d(&tm_k, 64, hkv, row, f.bcoord);
+          tma_prefetch_4d(&tm_v, 0, hkv, row, f.bcoord);
+          tma_prefetch_4d(&tm_v, 64, hkv, row, f.bcoord);
         });
       }
       if (*abort) {  // let loads still in flight land before the CTA exits
@@ -509,7 +548,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
               tma_load_4d(sV + st * kA2Tile + kA2Half, &tm_v, v_full + st, 64, hkv, vrow, f.bcoord);
               ++vseq;
               return true;
-            }))
+            }, [](int) {}))
           break;
       }
       if (*abort) {
@@ -766,12 +805,18 @@ __global__ void __launch_bounds__(kA2Threads, 1)
       float m_use = -INFINITY, l = 0.f;
       bool ok = true;
       for (int j = 0; j < n; ++j) {
-        if (!A2_W(0, mbar_wait_warp_sleep(s_full + t, sc & 1, abort))) { ok = false; break; }
+        if (!A2_W(0, A2_SM_WAIT(s_full + t, sc & 1, abort))) { ok = false; break; }
         ++sc;
         tc_fence_after();
         const unsigned long long tp0 = A2_CLK();
         (void)tp0;
         A2_EV(5, (t << 16) | j);
+        if (FPB_A2_TIMING_NOSOFTMAX) {  // timing experiment only: P = whatever S holds
+          tc_fence_before();
+          mbar_arrive(p_full + t);
+          l = 1.f;
+          continue;
+        }
         uint32_t u[128];
         tmem_ld32(t_s, *reinterpret_cast<uint32_t(*)[32]>(u));
         tmem_ld32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(u + 32));
@@ -842,7 +887,10 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         for (int k = 0; k < 64; ++k) {
           float x0, x1, p0, p1;
           fma2(x0, x1, __uint_as_float(u[2 * k]), __uint_as_float(u[2 * k + 1]), c, c, neg_m, neg_m);
-          if ((k % kA2PolyEvery) == kA2PolyEvery - 1) {
+          if (FPB_A2_TIMING_NOEXP) {  // timing experiment only: wrong results
+            p0 = x0;
+            p1 = x1;
+          } else if ((k % kA2PolyEvery) == kA2PolyEvery - 1) {
             exp2_poly2(x0, x1, p0, p1);  // masked (-inf) entries give 2^-126 here, negligible
           } else {
             p0 = ex2_approx(x0);
@@ -871,7 +919,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         (void)tp3;
         A2_ADD(3, tp3 - tp2);
         A2_ADD(6, 1);
-        if (__any_sync(0xffffffffu, scale_o != 1.f)) {
+        if (!FPB_A2_TIMING_NORESCALE && __any_sync(0xffffffffu, scale_o != 1.f)) {
           A2_ADD(7, 1);
           // O_t holds the blocks before this one (PV_t(previous) completed before S_t(this)
           // did); rescale this row before PV_t(this) may start (p_full below).  u[64..127]
