@@ -25,9 +25,13 @@
 //   warps 4-7     softmax + epilogue of tile 0 (one thread per query row, 128 columns)
 //   warps 8-11    softmax + epilogue of tile 1
 // TMEM columns: S_0 [0,128), S_1 [128,256), O_0 [256,384), O_1 [384,512).
-// Shared memory: Q_0, Q_1, K[2], V[2] (32 KB each, 128-byte swizzled) and the barriers.
-// The epilogue writes O / l from registers straight to global memory (each thread one row of
-// 256 contiguous bytes), so no staging tile holds back the next item's loads.
+// Shared memory: Q_0, Q_1, K[2], V[2] (32 KB each, 128-byte swizzled), 4 KB of output
+// staging per softmax warp, and the barriers.
+// The epilogue takes O / l from TMEM into registers and writes each warp's 32 rows through its
+// own staging area, half a row at a time, as whole 128-byte lines (a thread storing its own
+// 256-byte row makes every store instruction touch 32 lines, and that burst holds up the
+// shared-memory and barrier traffic of the producer and the MMA issuer at every item boundary).
+// The staging area is the warp's own, so it never holds back the next item's loads.
 #include <type_traits>
 
 #include "fp_common.cuh"
@@ -132,6 +136,11 @@ constexpr int kA2KStages = FPB_A2_KSTAGES, kA2VStages = 2;
 #ifndef FPB_A2_TIMING_NORESCALE
 #define FPB_A2_TIMING_NORESCALE 0
 #endif
+// Timing experiments only: 1 = no K/V tile loads (the full barriers are arrived without data),
+// 2 = every K/V load reads the sequence's first key block (always an L2 hit)
+#ifndef FPB_A2_TIMING_KV
+#define FPB_A2_TIMING_KV 0
+#endif
 // 1: the softmax warps poll for S without suspending (0: try_wait with a suspend-time hint)
 #ifndef FPB_A2_SM_SPIN
 #define FPB_A2_SM_SPIN 0
@@ -141,14 +150,30 @@ constexpr int kA2KStages = FPB_A2_KSTAGES, kA2VStages = 2;
 #else
 #define A2_SM_WAIT mbar_wait_warp_sleep
 #endif
+// 1: the K/V producer's waits spin (0: try_wait with a suspend-time hint)
+#ifndef FPB_A2_PROD_SPIN
+#define FPB_A2_PROD_SPIN 0
+#endif
+#if FPB_A2_PROD_SPIN
+#define A2_PROD_WAIT mbar_wait
+#else
+#define A2_PROD_WAIT mbar_wait_sleep
+#endif
 #if FPB_A2_MMA_SLEEP
 #define A2_MMA_WAIT mbar_wait_sleep
 #else
 #define A2_MMA_WAIT mbar_wait
 #endif
 constexpr bool kA2SplitProducer = FPB_A2_SPLIT_PRODUCER, kA2EarlyQFree = FPB_A2_EARLY_QFREE;
+// 1: the epilogue stages each warp's 32 output rows through shared memory, half a row at a
+// time, and stores them with consecutive lanes on consecutive 16-byte pieces of a row (whole
+// 128-byte lines); 0: each thread stores its own 256-byte row (32 lines per warp instruction)
+#ifndef FPB_A2_STAGE_OUT
+#define FPB_A2_STAGE_OUT 1
+#endif
+constexpr int kA2StageBytes = FPB_A2_STAGE_OUT ? 8 * 32 * 128 : 0;  // 8 softmax warps x 32 rows x 128 B
 __host__ __device__ constexpr size_t attn2_smem_bytes() {
-  return (size_t)kA2Tile * (2 + kA2KStages + kA2VStages) + 1024 + 1024;
+  return (size_t)kA2Tile * (2 + kA2KStages + kA2VStages) + kA2StageBytes + 1024 + 1024;
 }
 
 // Instrumentation (build flag -DFPB_ATTN_PROFILE=1, run time FLASHPREFILL_B200_PROFILE=1): cycle
@@ -246,7 +271,9 @@ __global__ void __launch_bounds__(kA2Threads, 1)
   uint8_t* sQ = smem;                               // [2] tiles
   uint8_t* sK = smem + 2 * kA2Tile;                 // [kA2KStages]
   uint8_t* sV = sK + kA2KStages * kA2Tile;          // [kA2VStages]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kA2VStages * kA2Tile);
+  uint8_t* sStage = sV + kA2VStages * kA2Tile;     // [softmax warp] 32 rows x 128 B (FPB_A2_STAGE_OUT)
+  (void)sStage;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + kA2StageBytes);
   uint64_t* item_full = bars + 0;   // [slot]
   uint64_t* item_empty = bars + 2;  // [slot]
   uint64_t* q_full = bars + 4;      // [tile]
@@ -389,9 +416,11 @@ __global__ void __launch_bounds__(kA2Threads, 1)
       bool ok = true;
       while (ok) {
         const int slot = it & 1;
-        if (!A2_W(20, mbar_wait_sleep(item_empty + slot, ((it >> 1) & 1) ^ 1, abort))) break;
+        if (!A2_W(20, A2_PROD_WAIT(item_empty + slot, ((it >> 1) & 1) ^ 1, abort))) break;
         Item2 f{};
+        A2_EV(20, it);
         const int id = atomicAdd(A.counter, 1);
+        A2_EV(21, id);
         const int32_t* lst[2] = {nullptr, nullptr};
         if (id >= n_ent + A.total_items) {
           f.valid = 0;
@@ -432,6 +461,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
               f.valid = 2;
           }
         }
+        A2_EV(22, f.n[0] + f.n[1]);
         ring[slot] = f;
         mbar_arrive(item_full + slot);
         ++it;
@@ -455,7 +485,8 @@ __global__ void __launch_bounds__(kA2Threads, 1)
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
             if (f.n[t] == 0) continue;
-            if (!A2_W(19, mbar_wait_sleep(q_empty + t, (qld[t] & 1) ^ 1, abort))) return false;
+            if (!A2_W(19, A2_PROD_WAIT(q_empty + t, (qld[t] & 1) ^ 1, abort))) return false;
+            A2_EV(23, t);
             ++qld[t];
             mbar_arrive_expect_tx(q_full + t, kA2Tile);
             tma_load_4d_hint(sQ + t * kA2Tile, &tm_q, q_full + t, 0, f.h[t], qrow, f.bcoord, stream_once);
@@ -468,7 +499,8 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         ok = walk_union(lst[0], f.n[0], lst[1], f.n[1], f.qb, [&](int kb, int m) -> bool {
           const int st = kseq % kA2KStages;
           const uint32_t ph = (kseq / kA2KStages) & 1;
-          if (!A2_W(17, mbar_wait_sleep(k_empty + st, ph ^ 1, abort))) return false;
+          A2_EV(24, kseq);
+          if (!A2_W(17, A2_PROD_WAIT(k_empty + st, ph ^ 1, abort))) return false;
           if (kA2Issuers == 2 && !A2_W(22, mbar_wait_sleep(k_empty1 + st, ph ^ 1, abort))) return false;
           umask[st] = m;
           // test hook (one-shot): the first producer to reach a key load while it is armed
@@ -476,8 +508,10 @@ __global__ void __launch_bounds__(kA2Threads, 1)
           bool withhold = false;
           if (kseq == 0 && *(volatile int*)&g_test_withhold != 0) withhold = atomicExch(&g_test_withhold, 0) != 0;
           A2_EV(7, kseq);
-          if (!withhold) {
-            const int krow = f.start + kb * kBlock;
+          if (FPB_A2_TIMING_KV == 1) {
+            mbar_arrive(k_full + st);
+          } else if (!withhold) {
+            const int krow = f.start + (FPB_A2_TIMING_KV == 2 ? 0 : kb) * kBlock;
             mbar_arrive_expect_tx(k_full + st, kA2Tile);
             tma_load_4d(sK + st * kA2Tile, &tm_k, k_full + st, 0, hkv, krow, f.bcoord);
             tma_load_4d(sK + st * kA2Tile + kA2Half, &tm_k, k_full + st, 64, hkv, krow, f.bcoord);
@@ -485,12 +519,16 @@ __global__ void __launch_bounds__(kA2Threads, 1)
           if (!kA2SplitProducer) {  // this thread loads the V tile too
             const int vs = kseq & 1;
             const uint32_t vph = ((kseq >> 1) & 1) ^ 1;
-            if (!A2_W(18, mbar_wait_sleep(v_empty + vs, vph, abort))) return false;
+            if (!A2_W(18, A2_PROD_WAIT(v_empty + vs, vph, abort))) return false;
             if (kA2Issuers == 2 && !A2_W(22, mbar_wait_sleep(v_empty1 + vs, vph, abort))) return false;
-            const int vrow = f.start + kb * kBlock;
-            mbar_arrive_expect_tx(v_full + vs, kA2Tile);
-            tma_load_4d(sV + vs * kA2Tile, &tm_v, v_full + vs, 0, hkv, vrow, f.bcoord);
-            tma_load_4d(sV + vs * kA2Tile + kA2Half, &tm_v, v_full + vs, 64, hkv, vrow, f.bcoord);
+            const int vrow = f.start + (FPB_A2_TIMING_KV == 2 ? 0 : kb) * kBlock;
+            if (FPB_A2_TIMING_KV == 1) {
+              mbar_arrive(v_full + vs);
+            } else {
+              mbar_arrive_expect_tx(v_full + vs, kA2Tile);
+              tma_load_4d(sV + vs * kA2Tile, &tm_v, v_full + vs, 0, hkv, vrow, f.bcoord);
+              tma_load_4d(sV + vs * kA2Tile + kA2Half, &tm_v, v_full + vs, 64, hkv, vrow, f.bcoord);
+            }
           }
           ++kseq;
           if (q_pending && !load_q()) return false;
@@ -998,7 +1036,37 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         continue;
       }
       const float inv = 1.f / l;
-      if (row_out) {
+      if (kA2StageBytes > 0) {
+        // lane = row; half h of the 32 rows goes through shared memory (piece q of a row at slot
+        // q ^ (row & 7), conflict-free both ways), then out four rows per store instruction
+        const uint64_t pol = l2_policy_evict_first();
+        uint4* stg = reinterpret_cast<uint4*>(sStage) + (warp - 4) * 256;
+        const unsigned vmask = __ballot_sync(0xffffffffu, row_out);
+        const long long mine = reinterpret_cast<long long>(orow);
+        long long rows[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rows[i] = __shfl_sync(0xffffffffu, mine, 4 * i + (lane >> 3));
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int q4 = h * 8 + q;
+            uint32_t pk[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              pk[i] = DT<T>::pack(__uint_as_float(o[q4 * 8 + 2 * i]) * inv, __uint_as_float(o[q4 * 8 + 2 * i + 1]) * inv);
+            stg[lane * 8 + (q ^ (lane & 7))] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          }
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int rr = 4 * i + (lane >> 3), pc = lane & 7;
+            if ((vmask >> rr) & 1u)
+              st_global_hint(reinterpret_cast<uint4*>(rows[i]) + h * 8 + pc, stg[rr * 8 + (pc ^ (rr & 7))], pol);
+          }
+          __syncwarp();
+        }
+      } else if (row_out) {
         const uint64_t pol = l2_policy_evict_first();  // the output is not read again here
         uint4* dst = reinterpret_cast<uint4*>(orow);
 #pragma unroll
