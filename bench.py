@@ -55,9 +55,9 @@ UNIT = "ms/layer"
 # block_search_persistent_kernel).  Reported as roofline traffic for those workloads on one GPU
 # with all heads; other runs (shards, N > 1, other workloads) report null.
 NCU_TRAFFIC = {
-    "llama3_8b_layer_128k": {"attention": 2119719424 + 1018989056,
-                             "search": 1074931200 + 4992000},
-    "cfg1_llama3_8b_32k": {"attention": 504239104 + 217063168,
+    "llama3_8b_layer_128k": {"attention": 2139156224 + 1015631104,
+                             "search": 1074930688 + 4879104},
+    "cfg1_llama3_8b_32k": {"attention": 504537344 + 221985536,
                            "search": 267095552 + 3992320},
 }
 
