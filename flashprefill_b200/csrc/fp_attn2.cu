@@ -63,10 +63,16 @@ struct Attn2Args {
   int64_t o_sb, o_ss, o_sh;  // output strides in elements
 };
 
+// 1: each tile's P goes to a shared-memory tile of its own instead of over S in TMEM, so S_t(next)
+// may be issued as soon as the softmax has read S_t into registers and runs under the softmax of
+// this block (the K ring then has one stage: Q, K, V[2], P[2] take 224 KB)
+#ifndef FPB_A2_PSMEM
+#define FPB_A2_PSMEM 0
+#endif
 constexpr int kA2Threads = 384;
 // Register split: compiled for 168 per thread (384 x 168 = 64512 <= 65536); warps 0-3 give back
 // to 80, the two softmax warpgroups grow to 208: 128 * 80 + 256 * 208 = 63488.
-constexpr int kA2LaunchRegs = 168, kA2RoleRegs = 80, kA2SoftRegs = 208;
+constexpr int kA2LaunchRegs = 168, kA2RoleRegs = FPB_A2_PSMEM ? 88 : 80, kA2SoftRegs = 208;
 static_assert(128 * kA2RoleRegs + 256 * kA2SoftRegs <= kA2Threads * kA2LaunchRegs, "register split");
 #ifndef FPB_A2_POLY_EVERY
 #define FPB_A2_POLY_EVERY 1000
@@ -91,7 +97,7 @@ constexpr uint32_t kA2Half = kA2Tile / 2;
 // after the item's last MMA 2.80 (after its last S 2.87); one MMA issuer 2.80 (one per tile
 // 3.17-3.58).  Every extra polling thread takes issue slots from the softmax warps.
 #ifndef FPB_A2_KSTAGES
-#define FPB_A2_KSTAGES 2
+#define FPB_A2_KSTAGES (FPB_A2_PSMEM ? 1 : 2)
 #endif
 // 1: a second producer thread (warp 2) loads the V tiles; 0: the K producer loads both
 #ifndef FPB_A2_SPLIT_PRODUCER
@@ -171,7 +177,12 @@ constexpr bool kA2SplitProducer = FPB_A2_SPLIT_PRODUCER, kA2EarlyQFree = FPB_A2_
 #ifndef FPB_A2_STAGE_OUT
 #define FPB_A2_STAGE_OUT 1
 #endif
-constexpr int kA2StageBytes = FPB_A2_STAGE_OUT ? 8 * 32 * 128 : 0;  // 8 softmax warps x 32 rows x 128 B
+constexpr bool kA2PSmem = FPB_A2_PSMEM;
+static_assert(!kA2PSmem || (!FPB_A2_TIMING_NOSOFTMAX && kA2Issuers == 1 && !kA2EarlyQFree),
+              "the shared-memory P pipeline has one MMA issuer and a full softmax");
+// the output staging areas (8 softmax warps x 32 rows x 128 B), or the two P tiles, whose halves
+// the warps of each tile use as staging areas
+constexpr int kA2StageBytes = FPB_A2_PSMEM ? 2 * (int)kA2Tile : FPB_A2_STAGE_OUT ? (int)kA2Tile : 0;
 __host__ __device__ constexpr size_t attn2_smem_bytes() {
   return (size_t)kA2Tile * (2 + kA2KStages + kA2VStages) + kA2StageBytes + 1024 + 1024;
 }
@@ -272,7 +283,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
   uint8_t* sK = smem + 2 * kA2Tile;                 // [kA2KStages]
   uint8_t* sV = sK + kA2KStages * kA2Tile;          // [kA2VStages]
   uint8_t* sStage = sV + kA2VStages * kA2Tile;     // [softmax warp] 32 rows x 128 B (FPB_A2_STAGE_OUT)
-  (void)sStage;
+  (void)sStage;                                     // FPB_A2_PSMEM: also the P tile (128 rows x 128 keys)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + kA2StageBytes);
   uint64_t* item_full = bars + 0;   // [slot]
   uint64_t* item_empty = bars + 2;  // [slot]
@@ -293,6 +304,8 @@ __global__ void __launch_bounds__(kA2Threads, 1)
   uint64_t* o_empty = bars + 22;
   uint64_t* mma_done = bars + 24;
   uint64_t* epi = bars + 25;        // [tile]: bounded sync of a tile's 128 softmax threads
+  uint64_t* s_free = bars + 64;     // [tile] (FPB_A2_PSMEM): the softmax has read S_t into registers
+  uint64_t* p_grant = bars + 66;    // [tile] (FPB_A2_PSMEM): P_t was read by its PV, P_t may be written
   Item2* ring = reinterpret_cast<Item2*>(bars + 32);          // [slot], 80 bytes each
   int* umask_raw = reinterpret_cast<int*>(ring + 2);
   volatile int* umask = umask_raw;  // [K stage]: tiles | last << 2
@@ -337,6 +350,8 @@ __global__ void __launch_bounds__(kA2Threads, 1)
       mbar_init(o_full + i, 1);
       mbar_init(o_empty + i, 128);
       mbar_init(epi + i, 128);
+      mbar_init(s_free + i, 128);
+      mbar_init(p_grant + i, 1);
     }
     mbar_init(mma_done, kA2Issuers);
     for (int i = 0; i < 12; ++i) pp_want[i] = 0;  // want flags, then the turn and two exit counters
@@ -688,7 +703,114 @@ __global__ void __launch_bounds__(kA2Threads, 1)
       umma_commit(mma_done);
       volatile int no_abort = 0;
       mbar_wait(mma_done, 0, &no_abort);
-    } else if (kA2Issuers == 1 && warp == 1 && lane == 0) {
+    } else if (kA2PSmem && warp == 1 && lane == 0) {
+      // ------------------------------------------------------------ MMA issuer, P in shared memory
+      // Per union block: S_0 and S_1 of this block (each once the softmax has read the tile's
+      // previous S), then PV_0 and PV_1 of the previous block.  Each PV_t is followed by a commit
+      // to p_grant_t: it arrives once that PV has read P_t, and the softmax writes P_t again only
+      // after it.
+      constexpr uint32_t id_s = idesc_f16(128, 128, DT<T>::is_bf16, false);
+      constexpr uint32_t id_o = idesc_f16(128, 128, DT<T>::is_bf16, true);
+      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV), p_base = smem_u32(sStage);
+      uint32_t it = 0, kvseq = 0, qc[2] = {0, 0}, pc[2] = {0, 0}, oc[2] = {0, 0}, sf[2] = {0, 0}, ns[2] = {0, 0};
+      int users0 = 0, users1 = 0;  // PVs still to be issued on the V tile of stage 0 / 1
+      using T0 = std::integral_constant<int, 0>;
+      using T1 = std::integral_constant<int, 1>;
+      bool ok = true;
+      while (ok) {
+        const int slot = it & 1;
+        if (!A2_W(16, mbar_wait_sleep(item_full + slot, (it >> 1) & 1, abort))) break;
+        const int valid = ring[slot].valid, n0 = ring[slot].n[0], n1 = ring[slot].n[1];
+        mbar_arrive(item_empty + slot);
+        ++it;
+        if (valid == 0) break;
+        if (valid != 1 || (n0 == 0 && n1 == 0)) continue;
+        int pend[2] = {-1, -1};  // union sequence number of the block whose PV is due
+        bool first[2] = {true, true}, qw[2] = {false, false};
+        auto issue_pv = [&](auto tt) -> bool {
+          constexpr int t = decltype(tt)::value;
+          const int q = pend[t], st = q & 1;
+          if (first[t]) {  // the previous item's epilogue must have read O_t
+            if (!A2_W(12, A2_MMA_WAIT(o_empty + t, (oc[t] & 1) ^ 1, abort))) return false;
+            ++oc[t];
+          }
+          if (!A2_W(10, A2_MMA_WAIT(p_full + t, pc[t] & 1, abort))) return false;
+          ++pc[t];
+          if (!A2_W(11, A2_MMA_WAIT(v_full + st, (q >> 1) & 1, abort))) return false;
+          tc_fence_after();
+          constexpr uint32_t t_o = 256 + t * 128;
+          const uint32_t vb = v_base + st * kA2Tile;
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {  // A = P_t (shared memory, K-major like Q), B = V (MN-major)
+            const uint32_t off = t * kA2Tile + (ks >> 2) * kA2Half + (ks & 3) * 32;
+            umma_ss(tmem + t_o, sdesc_sw128(p_base + off, 16, 1024), sdesc_sw128(vb + ks * 2048, kA2Half, 1024), id_o,
+                    (!first[t] || ks > 0) ? 1u : 0u);
+          }
+          umma_commit(p_grant + t);
+          first[t] = false;
+          if (st == 0) {
+            if (--users0 == 0) umma_commit(v_empty);
+          } else {
+            if (--users1 == 0) umma_commit(v_empty + 1);
+          }
+          pend[t] = -1;
+          return true;
+        };
+        auto issue_s = [&](auto tt, int st) -> bool {
+          constexpr int t = decltype(tt)::value;
+          if (!qw[t]) {
+            if (!A2_W(13, A2_MMA_WAIT(q_full + t, qc[t] & 1, abort))) return false;
+            ++qc[t];
+            qw[t] = true;
+          }
+          if (ns[t] > 0) {  // S_t is free once the softmax has read the previous S_t
+            if (!A2_W(10, A2_MMA_WAIT(s_free + t, sf[t] & 1, abort))) return false;
+            ++sf[t];
+          }
+          ++ns[t];
+          tc_fence_after();
+          const uint32_t qb_ = q_base + t * kA2Tile, kb_ = k_base + st * kA2Tile;
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t off = (ks >> 2) * kA2Half + (ks & 3) * 32;
+            umma_ss(tmem + t * 128, sdesc_sw128(qb_ + off, 16, 1024), sdesc_sw128(kb_ + off, 16, 1024), id_s,
+                    ks > 0);
+          }
+          umma_commit(s_full + t);
+          return true;
+        };
+        bool last = false;
+        while (!last && ok) {
+          const int ks_ = kvseq % kA2KStages, st = kvseq & 1;  // K stage, V stage of this union block
+          if (!A2_W(9, A2_MMA_WAIT(k_full + ks_, (kvseq / kA2KStages) & 1, abort))) { ok = false; break; }
+          const int m = umask[ks_];
+          last = (m & 4) != 0;
+          if ((m & 1) && !issue_s(T0{}, ks_)) { ok = false; break; }
+          if ((m & 2) && !issue_s(T1{}, ks_)) { ok = false; break; }
+          umma_commit(k_empty + ks_);
+          if (pend[0] >= 0 && !issue_pv(T0{})) { ok = false; break; }
+          if (pend[1] >= 0 && !issue_pv(T1{})) { ok = false; break; }
+          if (m & 1) pend[0] = (int)kvseq;
+          if (m & 2) pend[1] = (int)kvseq;
+          if (st == 0) users0 = __popc(m & 3); else users1 = __popc(m & 3);
+          ++kvseq;
+        }
+        if (!ok) break;
+        if (pend[0] >= 0 && !issue_pv(T0{})) break;
+        if (pend[1] >= 0 && !issue_pv(T1{})) break;
+        if (n0 > 0) {
+          umma_commit(o_full);
+          umma_commit(q_empty);
+        }
+        if (n1 > 0) {
+          umma_commit(o_full + 1);
+          umma_commit(q_empty + 1);
+        }
+      }
+      umma_commit(mma_done);
+      volatile int no_abort = 0;
+      mbar_wait(mma_done, 0, &no_abort);
+    } else if (kA2Issuers == 1 && !kA2PSmem && warp == 1 && lane == 0) {
       // ------------------------------------------------------------ MMA issuer
       constexpr uint32_t id_s = idesc_f16(128, 128, DT<T>::is_bf16, false);
       constexpr uint32_t id_o = idesc_f16(128, 128, DT<T>::is_bf16, true);
@@ -808,7 +930,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
     const uint32_t t_s = tmem + t * 128 + lane_off;
     const uint32_t t_o = tmem + 256 + t * 128 + lane_off;
     const float c = A.c;
-    uint32_t it = 0, sc = 0, oc = 0, ep = 0;
+    uint32_t it = 0, sc = 0, oc = 0, ep = 0, pw = 0;
     auto group_sync = [&]() -> bool {  // the tile's 128 softmax threads, bounded
       mbar_arrive(epi + t);
       return A2_W(22, mbar_wait_warp_sleep(epi + t, (ep++) & 1, abort));
@@ -861,6 +983,10 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         tmem_ld32(t_s + 64, *reinterpret_cast<uint32_t(*)[32]>(u + 64));
         tmem_ld32(t_s + 96, *reinterpret_cast<uint32_t(*)[32]>(u + 96));
         tmem_ld_wait();
+        if (kA2PSmem) {  // S_t is in registers: the next S_t may be issued
+          tc_fence_before();
+          mbar_arrive(s_free + t);
+        }
         const unsigned long long tp1 = A2_CLK();
         (void)tp1;
         A2_ADD(1, tp1 - tp0);
@@ -951,8 +1077,21 @@ __global__ void __launch_bounds__(kA2Threads, 1)
           if (atomicAdd(const_cast<int*>(pp_turn) + 1 + t, 1) % 4 == 3) pp_turn[0] = 1 - t;  // last of 4 warps
         }
 #endif
-        tmem_st32(t_s, *reinterpret_cast<uint32_t(*)[32]>(u));
-        tmem_st32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(u + 32));
+        if (kA2PSmem) {
+          // P_t may be written once its last PV has read it (p_grant_t; the first write of the
+          // launch has none before it).  Row r in the TMA layout of a K-major 128-byte-swizzled
+          // tile: keys [64h, 64h+64) at h * 16 KB + r * 128, 16-byte piece c at (c ^ (r & 7)) * 16
+          if (pw > 0 && !A2_W(5, mbar_wait_warp(p_grant + t, (pw - 1) & 1, abort))) { ok = false; break; }
+          ++pw;
+          uint4* prow = reinterpret_cast<uint4*>(sStage + t * kA2Tile + r * 128);
+#pragma unroll
+          for (int c16 = 0; c16 < 16; ++c16)
+            prow[(c16 >> 3) * (kA2Half / 16) + ((c16 & 7) ^ (r & 7))] =
+                make_uint4(u[4 * c16], u[4 * c16 + 1], u[4 * c16 + 2], u[4 * c16 + 3]);
+        } else {
+          tmem_st32(t_s, *reinterpret_cast<uint32_t(*)[32]>(u));
+          tmem_st32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(u + 32));
+        }
         const unsigned long long tp3 = A2_CLK();
         (void)tp3;
         A2_ADD(3, tp3 - tp2);
@@ -984,6 +1123,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         A2_ADD(4, tp4 - tp3);
         tmem_st_wait();
         l += rs0 + rs1;
+        if (kA2PSmem) fence_proxy_async_smem();  // P (generic-proxy stores) visible to the MMA
         tc_fence_before();
         mbar_arrive(p_full + t);
         A2_EV(6, (t << 16) | j);
@@ -1040,7 +1180,9 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         // lane = row; half h of the 32 rows goes through shared memory (piece q of a row at slot
         // q ^ (row & 7), conflict-free both ways), then out four rows per store instruction
         const uint64_t pol = l2_policy_evict_first();
-        uint4* stg = reinterpret_cast<uint4*>(sStage) + (warp - 4) * 256;
+        // tile t's warps use [t * half, (t + 1) * half) of the area (with P in shared memory:
+        // of P_t, which its last PV has read: o_full_t is committed after it)
+        uint4* stg = reinterpret_cast<uint4*>(sStage + t * (kA2StageBytes / 2)) + quad * 256;
         const unsigned vmask = __ballot_sync(0xffffffffu, row_out);
         const long long mine = reinterpret_cast<long long>(orow);
         long long rows[8];
