@@ -705,17 +705,18 @@ __global__ void __launch_bounds__(kA2Threads, 1)
       mbar_wait(mma_done, 0, &no_abort);
     } else if (kA2PSmem && warp == 1 && lane == 0) {
       // ------------------------------------------------------------ MMA issuer, P in shared memory
-      // Per union block: S_0 and S_1 of this block (each once the softmax has read the tile's
-      // previous S), then PV_0 and PV_1 of the previous block.  Each PV_t is followed by a commit
-      // to p_grant_t: it arrives once that PV has read P_t, and the softmax writes P_t again only
-      // after it.
+      // Two cursors over the item's union blocks, each advanced as soon as its barriers have
+      // completed (non-blocking probes, one bounded clock for the whole item):
+      //   S cursor:  S_0, S_1 of block s (K(s) loaded; S_t free: the softmax has read S_t), then
+      //              k_empty; it runs at most two blocks ahead of the PV cursor;
+      //   PV cursor: PV_0, PV_1 of block v < s (P_t written; V(v) loaded; O_t read by the last
+      //              epilogue for the item's first PV_t), each followed by a commit to p_grant_t
+      //              (P_t may be written again), then v_empty.
       constexpr uint32_t id_s = idesc_f16(128, 128, DT<T>::is_bf16, false);
       constexpr uint32_t id_o = idesc_f16(128, 128, DT<T>::is_bf16, true);
       const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV), p_base = smem_u32(sStage);
+      volatile int* imask = reinterpret_cast<volatile int*>(tmem_slot + 16);  // [block & 3] masks between the cursors
       uint32_t it = 0, kvseq = 0, qc[2] = {0, 0}, pc[2] = {0, 0}, oc[2] = {0, 0}, sf[2] = {0, 0}, ns[2] = {0, 0};
-      int users0 = 0, users1 = 0;  // PVs still to be issued on the V tile of stage 0 / 1
-      using T0 = std::integral_constant<int, 0>;
-      using T1 = std::integral_constant<int, 1>;
       bool ok = true;
       while (ok) {
         const int slot = it & 1;
@@ -725,79 +726,104 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         ++it;
         if (valid == 0) break;
         if (valid != 1 || (n0 == 0 && n1 == 0)) continue;
-        int pend[2] = {-1, -1};  // union sequence number of the block whose PV is due
-        bool first[2] = {true, true}, qw[2] = {false, false};
-        auto issue_pv = [&](auto tt) -> bool {
-          constexpr int t = decltype(tt)::value;
-          const int q = pend[t], st = q & 1;
-          if (first[t]) {  // the previous item's epilogue must have read O_t
-            if (!A2_W(12, A2_MMA_WAIT(o_empty + t, (oc[t] & 1) ^ 1, abort))) return false;
-            ++oc[t];
-          }
-          if (!A2_W(10, A2_MMA_WAIT(p_full + t, pc[t] & 1, abort))) return false;
-          ++pc[t];
-          if (!A2_W(11, A2_MMA_WAIT(v_full + st, (q >> 1) & 1, abort))) return false;
-          tc_fence_after();
-          constexpr uint32_t t_o = 256 + t * 128;
-          const uint32_t vb = v_base + st * kA2Tile;
+        const uint32_t base = kvseq;                  // sequence number of the item's first block
+        uint32_t sq = base, vq = base, s_end = 0xffffffffu;  // s_end: one past the item's last block
+        int s_t = 0, v_t = 0;                         // next tile within the cursor's block
+        bool k_ready = false, qw0 = false, qw1 = false, first0 = true, first1 = true;
+        int ms = 0;
+        const uint64_t lim = g_wait_limit_ns;
+        uint64_t t_last = global_timer_ns();
+        uint32_t polls = 0;
+        while (vq != s_end) {
+          bool moved = false;
+          // ---- S cursor
+          if (sq != s_end && sq - vq < 2) {
+            const int ks_ = sq % kA2KStages;
+            if (!k_ready && mbar_probe(k_full + ks_, (sq / kA2KStages) & 1)) {
+              ms = umask[ks_];
+              imask[sq & 3] = ms;
+              k_ready = true;
+            }
+            while (k_ready && s_t < 2) {
+              if (!((ms >> s_t) & 1)) { ++s_t; continue; }
+              const int t = s_t;
+              const bool qready = t ? qw1 : qw0;
+              if (!qready) {
+                if (!mbar_probe(q_full + t, qc[t] & 1)) break;
+                ++qc[t];
+                if (t) qw1 = true; else qw0 = true;
+              }
+              if (ns[t] > 0) {
+                if (!mbar_probe(s_free + t, sf[t] & 1)) break;
+                ++sf[t];
+              }
+              ++ns[t];
+              tc_fence_after();
+              const uint32_t qb_ = q_base + t * kA2Tile, kb_ = k_base + ks_ * kA2Tile;
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {  // A = P_t (shared memory, K-major like Q), B = V (MN-major)
-            const uint32_t off = t * kA2Tile + (ks >> 2) * kA2Half + (ks & 3) * 32;
-            umma_ss(tmem + t_o, sdesc_sw128(p_base + off, 16, 1024), sdesc_sw128(vb + ks * 2048, kA2Half, 1024), id_o,
-                    (!first[t] || ks > 0) ? 1u : 0u);
+              for (int ks = 0; ks < 8; ++ks) {
+                const uint32_t off = (ks >> 2) * kA2Half + (ks & 3) * 32;
+                umma_ss(tmem + t * 128, sdesc_sw128(qb_ + off, 16, 1024), sdesc_sw128(kb_ + off, 16, 1024), id_s,
+                        ks > 0);
+              }
+              umma_commit(s_full + t);
+              ++s_t;
+              moved = true;
+            }
+            if (k_ready && s_t == 2) {
+              umma_commit(k_empty + ks_);
+              if (ms & 4) s_end = sq + 1;
+              ++sq;
+              s_t = 0;
+              k_ready = false;
+              moved = true;
+            }
           }
-          umma_commit(p_grant + t);
-          first[t] = false;
-          if (st == 0) {
-            if (--users0 == 0) umma_commit(v_empty);
-          } else {
-            if (--users1 == 0) umma_commit(v_empty + 1);
-          }
-          pend[t] = -1;
-          return true;
-        };
-        auto issue_s = [&](auto tt, int st) -> bool {
-          constexpr int t = decltype(tt)::value;
-          if (!qw[t]) {
-            if (!A2_W(13, A2_MMA_WAIT(q_full + t, qc[t] & 1, abort))) return false;
-            ++qc[t];
-            qw[t] = true;
-          }
-          if (ns[t] > 0) {  // S_t is free once the softmax has read the previous S_t
-            if (!A2_W(10, A2_MMA_WAIT(s_free + t, sf[t] & 1, abort))) return false;
-            ++sf[t];
-          }
-          ++ns[t];
-          tc_fence_after();
-          const uint32_t qb_ = q_base + t * kA2Tile, kb_ = k_base + st * kA2Tile;
+          // ---- PV cursor
+          if (vq != sq) {
+            const int mv = imask[vq & 3], st = vq & 1;
+            while (v_t < 2) {
+              if (!((mv >> v_t) & 1)) { ++v_t; continue; }
+              const int t = v_t;
+              const bool fst = t ? first1 : first0;
+              if (fst && !mbar_probe(o_empty + t, (oc[t] & 1) ^ 1)) break;
+              if (!mbar_probe(p_full + t, pc[t] & 1)) break;
+              if (!mbar_probe(v_full + st, (vq >> 1) & 1)) break;
+              if (fst) ++oc[t];
+              ++pc[t];
+              tc_fence_after();
+              const uint32_t t_o = 256 + t * 128, vb = v_base + st * kA2Tile;
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
-            const uint32_t off = (ks >> 2) * kA2Half + (ks & 3) * 32;
-            umma_ss(tmem + t * 128, sdesc_sw128(qb_ + off, 16, 1024), sdesc_sw128(kb_ + off, 16, 1024), id_s,
-                    ks > 0);
+              for (int ks = 0; ks < 8; ++ks) {  // A = P_t (shared memory, K-major like Q), B = V (MN-major)
+                const uint32_t off = t * kA2Tile + (ks >> 2) * kA2Half + (ks & 3) * 32;
+                umma_ss(tmem + t_o, sdesc_sw128(p_base + off, 16, 1024), sdesc_sw128(vb + ks * 2048, kA2Half, 1024),
+                        id_o, (!fst || ks > 0) ? 1u : 0u);
+              }
+              umma_commit(p_grant + t);
+              if (t) first1 = false; else first0 = false;
+              ++v_t;
+              moved = true;
+            }
+            if (v_t == 2) {
+              umma_commit(v_empty + st);  // both of the block's PVs are issued
+              ++vq;
+              v_t = 0;
+              moved = true;
+            }
           }
-          umma_commit(s_full + t);
-          return true;
-        };
-        bool last = false;
-        while (!last && ok) {
-          const int ks_ = kvseq % kA2KStages, st = kvseq & 1;  // K stage, V stage of this union block
-          if (!A2_W(9, A2_MMA_WAIT(k_full + ks_, (kvseq / kA2KStages) & 1, abort))) { ok = false; break; }
-          const int m = umask[ks_];
-          last = (m & 4) != 0;
-          if ((m & 1) && !issue_s(T0{}, ks_)) { ok = false; break; }
-          if ((m & 2) && !issue_s(T1{}, ks_)) { ok = false; break; }
-          umma_commit(k_empty + ks_);
-          if (pend[0] >= 0 && !issue_pv(T0{})) { ok = false; break; }
-          if (pend[1] >= 0 && !issue_pv(T1{})) { ok = false; break; }
-          if (m & 1) pend[0] = (int)kvseq;
-          if (m & 2) pend[1] = (int)kvseq;
-          if (st == 0) users0 = __popc(m & 3); else users1 = __popc(m & 3);
-          ++kvseq;
+          if (moved) {
+            polls = 0;
+            t_last = global_timer_ns();
+          } else if (++polls % kTimerEvery == 0) {
+            if (*abort || global_timer_ns() - t_last > lim) {
+              *abort = 1;
+              ok = false;
+              break;
+            }
+          }
         }
+        kvseq = sq;
         if (!ok) break;
-        if (pend[0] >= 0 && !issue_pv(T0{})) break;
-        if (pend[1] >= 0 && !issue_pv(T1{})) break;
         if (n0 > 0) {
           umma_commit(o_full);
           umma_commit(q_empty);
