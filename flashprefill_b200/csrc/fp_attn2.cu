@@ -165,8 +165,14 @@ constexpr int kA2KStages = FPB_A2_KSTAGES, kA2VStages = 2;
 #else
 #define A2_PROD_WAIT mbar_wait_sleep
 #endif
+// 1: the MMA issuer polls with mbarrier.test_wait (never suspends) instead of try_wait
+#ifndef FPB_A2_MMA_PROBE
+#define FPB_A2_MMA_PROBE 0
+#endif
 #if FPB_A2_MMA_SLEEP
 #define A2_MMA_WAIT mbar_wait_sleep
+#elif FPB_A2_MMA_PROBE
+#define A2_MMA_WAIT mbar_wait_probe
 #else
 #define A2_MMA_WAIT mbar_wait
 #endif
@@ -178,6 +184,12 @@ constexpr bool kA2SplitProducer = FPB_A2_SPLIT_PRODUCER, kA2EarlyQFree = FPB_A2_
 #define FPB_A2_STAGE_OUT 1
 #endif
 constexpr bool kA2PSmem = FPB_A2_PSMEM;
+// 1: the softmax warps signal p_full / s_free / o_empty with one arrival per warp (lane 0, after
+// the warp has synchronised) instead of one per thread: 4 arrivals per tile instead of 128
+#ifndef FPB_A2_WARP_ARRIVE
+#define FPB_A2_WARP_ARRIVE 0
+#endif
+constexpr int kA2RowArrivals = FPB_A2_WARP_ARRIVE ? 4 : 128;
 static_assert(!kA2PSmem || (!FPB_A2_TIMING_NOSOFTMAX && kA2Issuers == 1 && !kA2EarlyQFree),
               "the shared-memory P pipeline has one MMA issuer and a full softmax");
 // the output staging areas (8 softmax warps x 32 rows x 128 B), or the two P tiles, whose halves
@@ -346,11 +358,11 @@ __global__ void __launch_bounds__(kA2Threads, 1)
       mbar_init(v_empty + i, 1);
       mbar_init(v_empty1 + i, 1);
       mbar_init(s_full + i, 1);
-      mbar_init(p_full + i, 128);
+      mbar_init(p_full + i, kA2RowArrivals);
       mbar_init(o_full + i, 1);
-      mbar_init(o_empty + i, 128);
+      mbar_init(o_empty + i, kA2RowArrivals);
       mbar_init(epi + i, 128);
-      mbar_init(s_free + i, 128);
+      mbar_init(s_free + i, kA2RowArrivals);
       mbar_init(p_grant + i, 1);
     }
     mbar_init(mma_done, kA2Issuers);
@@ -957,6 +969,16 @@ __global__ void __launch_bounds__(kA2Threads, 1)
     const uint32_t t_o = tmem + 256 + t * 128 + lane_off;
     const float c = A.c;
     uint32_t it = 0, sc = 0, oc = 0, ep = 0, pw = 0;
+    // a tile's per-row event: every thread's arrival, or (FPB_A2_WARP_ARRIVE) the warp's, once all
+    // its lanes are past their fences
+    auto row_arrive = [&](uint64_t* bar) {
+      if (kA2RowArrivals == 128) {
+        mbar_arrive(bar);
+      } else {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar);
+      }
+    };
     auto group_sync = [&]() -> bool {  // the tile's 128 softmax threads, bounded
       mbar_arrive(epi + t);
       return A2_W(22, mbar_wait_warp_sleep(epi + t, (ep++) & 1, abort));
@@ -999,7 +1021,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         A2_EV(5, (t << 16) | j);
         if (FPB_A2_TIMING_NOSOFTMAX) {  // timing experiment only: P = whatever S holds
           tc_fence_before();
-          mbar_arrive(p_full + t);
+          row_arrive(p_full + t);
           l = 1.f;
           continue;
         }
@@ -1011,7 +1033,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         tmem_ld_wait();
         if (kA2PSmem) {  // S_t is in registers: the next S_t may be issued
           tc_fence_before();
-          mbar_arrive(s_free + t);
+          row_arrive(s_free + t);
         }
         const unsigned long long tp1 = A2_CLK();
         (void)tp1;
@@ -1151,7 +1173,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         l += rs0 + rs1;
         if (kA2PSmem) fence_proxy_async_smem();  // P (generic-proxy stores) visible to the MMA
         tc_fence_before();
-        mbar_arrive(p_full + t);
+        row_arrive(p_full + t);
         A2_EV(6, (t << 16) | j);
         A2_ADD(5, A2_CLK() - tp4);
       }
@@ -1169,7 +1191,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
       tmem_ld32(t_o + 96, *reinterpret_cast<uint32_t(*)[32]>(o + 96));
       tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(o_empty + t);  // O_t may be overwritten by the next item's first PV
+      row_arrive(o_empty + t);  // O_t may be overwritten by the next item's first PV
       if (chunk >= 0) {  // a chunk of a split row: store the partial, the row's last chunk merges
         const int code = chunk;
         const int entry = code & (kSplitMaxEntries - 1), cix = (code >> 17) & 127;

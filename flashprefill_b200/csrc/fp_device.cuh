@@ -116,6 +116,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// The same with non-blocking probes (mbarrier.test_wait) instead of try_wait.
+__device__ __forceinline__ bool mbar_wait_probe(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (mbar_probe(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns(), lim = g_wait_limit_ns;
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_probe(bar, parity)) return true;
+    if (i % kTimerEvery == 0) {
+      if (*abort) return false;
+      if (global_timer_ns() - t0 > lim) {
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
 // Bounded wait that sleeps between polls (for waits that are usually long).
 __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_test_sleep(bar, parity, kSleepHintNs)) return true;
