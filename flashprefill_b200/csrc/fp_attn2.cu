@@ -194,9 +194,21 @@ static_assert(!kA2PSmem || (!FPB_A2_TIMING_NOSOFTMAX && kA2Issuers == 1 && !kA2E
               "the shared-memory P pipeline has one MMA issuer and a full softmax");
 // the output staging areas (8 softmax warps x 32 rows x 128 B), or the two P tiles, whose halves
 // the warps of each tile use as staging areas
-constexpr int kA2StageBytes = FPB_A2_PSMEM ? 2 * (int)kA2Tile : FPB_A2_STAGE_OUT ? (int)kA2Tile : 0;
+// 1: three Q buffers.  Tile 1's Q always uses buffer 2; tile 0's alternates between buffers 0
+// and 1 from one item to the next, so the producer loads the next item's Q_0 while this item
+// runs, and the item's epilogue stages its output rows in its own Q_0 buffer (free once its
+// MMAs are done).  The producer reuses a Q_0 buffer after the epilogue of the item two back.
+#ifndef FPB_A2_QROT
+#define FPB_A2_QROT 0
+#endif
+constexpr bool kA2QRot = FPB_A2_QROT;
+static_assert(!kA2QRot || (!kA2PSmem && kA2Issuers == 1 && !kA2EarlyQFree && !kA2KFirst && !kA2SplitProducer),
+              "the rotating Q buffers run with the default pipeline");
+constexpr int kA2QTiles = kA2QRot ? 3 : 2;
+constexpr int kA2StageBytes =
+    FPB_A2_PSMEM ? 2 * (int)kA2Tile : (FPB_A2_STAGE_OUT && !FPB_A2_QROT) ? (int)kA2Tile : 0;
 __host__ __device__ constexpr size_t attn2_smem_bytes() {
-  return (size_t)kA2Tile * (2 + kA2KStages + kA2VStages) + kA2StageBytes + 1024 + 1024;
+  return (size_t)kA2Tile * (kA2QTiles + kA2KStages + kA2VStages) + kA2StageBytes + 1024 + 1024;
 }
 
 // Instrumentation (build flag -DFPB_ATTN_PROFILE=1, run time FLASHPREFILL_B200_PROFILE=1): cycle
@@ -291,8 +303,8 @@ __global__ void __launch_bounds__(kA2Threads, 1)
                         const __grid_constant__ CUtensorMap tm_v, const Attn2Args A) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                               // [2] tiles
-  uint8_t* sK = smem + 2 * kA2Tile;                 // [kA2KStages]
+  uint8_t* sQ = smem;                               // [kA2QTiles] tiles
+  uint8_t* sK = smem + kA2QTiles * kA2Tile;         // [kA2KStages]
   uint8_t* sV = sK + kA2KStages * kA2Tile;          // [kA2VStages]
   uint8_t* sStage = sV + kA2VStages * kA2Tile;     // [softmax warp] 32 rows x 128 B (FPB_A2_STAGE_OUT)
   (void)sStage;                                     // FPB_A2_PSMEM: also the P tile (128 rows x 128 keys)
@@ -318,6 +330,8 @@ __global__ void __launch_bounds__(kA2Threads, 1)
   uint64_t* epi = bars + 25;        // [tile]: bounded sync of a tile's 128 softmax threads
   uint64_t* s_free = bars + 64;     // [tile] (FPB_A2_PSMEM): the softmax has read S_t into registers
   uint64_t* p_grant = bars + 66;    // [tile] (FPB_A2_PSMEM): P_t was read by its PV, P_t may be written
+  uint64_t* q_full_b = bars + 70;   // (FPB_A2_QROT): Q buffer 2 (tile 1) loaded; q_full[0/1]: buffers 0/1
+  uint64_t* stg_done = bars + 71;   // [Q_0 buffer] (FPB_A2_QROT): every softmax thread is past an item
   Item2* ring = reinterpret_cast<Item2*>(bars + 32);          // [slot], 80 bytes each
   int* umask_raw = reinterpret_cast<int*>(ring + 2);
   volatile int* umask = umask_raw;  // [K stage]: tiles | last << 2
@@ -364,7 +378,9 @@ __global__ void __launch_bounds__(kA2Threads, 1)
       mbar_init(epi + i, 128);
       mbar_init(s_free + i, kA2RowArrivals);
       mbar_init(p_grant + i, 1);
+      mbar_init(stg_done + i, 256);
     }
+    mbar_init(q_full_b, 1);
     mbar_init(mma_done, kA2Issuers);
     for (int i = 0; i < 12; ++i) pp_want[i] = 0;  // want flags, then the turn and two exit counters
     *abort = 0;
@@ -437,6 +453,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
       prefetch_tmap(&tm_k);
       const uint64_t stream_once = l2_policy_evict_first();
       uint32_t it = 0, kseq = 0, qld[2] = {0, 0};
+      uint32_t pq = 0, qldx0 = 0, qldx1 = 0;  // FPB_A2_QROT: items started, loads per Q_0 buffer
       // chunks of split rows come first in the work order (they are the longest work)
       const int n_ent = A.split ? A.sp_head[0] : 0;
       const int split_thr = A.split ? A.sp_head[3] : 0x7fffffff;  // only rows above it can be split
@@ -522,7 +539,34 @@ __global__ void __launch_bounds__(kA2Threads, 1)
           }
           return true;
         };
-        if (!kA2KFirst && !load_q()) break;
+        // FPB_A2_QROT: Q_0 into buffer pq & 1 once the epilogue of the item two back is done;
+        // Q_1 into buffer 2 after the item's first K/V, once the last item's MMAs are done
+        auto load_q0 = [&]() -> bool {
+          if (f.n[0] == 0) return true;
+          const int xs = pq & 1;
+          if (pq >= 2 && !A2_W(19, A2_PROD_WAIT(stg_done + xs, ((pq - 2) >> 1) & 1, abort))) return false;
+          if (xs) ++qldx1; else ++qldx0;
+          mbar_arrive_expect_tx(q_full + xs, kA2Tile);
+          tma_load_4d_hint(sQ + xs * kA2Tile, &tm_q, q_full + xs, 0, f.h[0], qrow, f.bcoord, stream_once);
+          tma_load_4d_hint(sQ + xs * kA2Tile + kA2Half, &tm_q, q_full + xs, 64, f.h[0], qrow, f.bcoord,
+                           stream_once);
+          return true;
+        };
+        auto load_q1 = [&]() -> bool {
+          q_pending = false;
+          if (f.n[1] == 0) return true;
+          if (!A2_W(19, A2_PROD_WAIT(q_empty + 1, (qld[1] & 1) ^ 1, abort))) return false;
+          ++qld[1];
+          mbar_arrive_expect_tx(q_full_b, kA2Tile);
+          tma_load_4d_hint(sQ + 2 * kA2Tile, &tm_q, q_full_b, 0, f.h[1], qrow, f.bcoord, stream_once);
+          tma_load_4d_hint(sQ + 2 * kA2Tile + kA2Half, &tm_q, q_full_b, 64, f.h[1], qrow, f.bcoord, stream_once);
+          return true;
+        };
+        if (kA2QRot) {
+          if (!load_q0()) break;
+        } else if (!kA2KFirst && !load_q()) {
+          break;
+        }
         ok = walk_union(lst[0], f.n[0], lst[1], f.n[1], f.qb, [&](int kb, int m) -> bool {
           const int st = kseq % kA2KStages;
           const uint32_t ph = (kseq / kA2KStages) & 1;
@@ -558,7 +602,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
             }
           }
           ++kseq;
-          if (q_pending && !load_q()) return false;
+          if (q_pending && !(kA2QRot ? load_q1() : load_q())) return false;
           return true;
         }, [&](int kb) {  // L2 prefetch of a block's K and V tiles, kA2Ahead list entries ahead
           if (kb < 0 || kb > f.qb) return;
@@ -568,6 +612,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
           tma_prefetch_4d(&tm_v, 0, hkv, row, f.bcoord);
           tma_prefetch_4d(&tm_v, 64, hkv, row, f.bcoord);
         });
+        ++pq;
       }
       if (*abort) {  // let loads still in flight land before the CTA exits
         volatile int no_abort = 0;
@@ -580,11 +625,20 @@ __global__ void __launch_bounds__(kA2Threads, 1)
             mbar_wait(v_full + (q & 1), (q >> 1) & 1, &no_abort);
             no_abort = 0;
           }
-        for (int t = 0; t < 2; ++t)
-          if (qld[t]) {
-            mbar_wait(q_full + t, (qld[t] - 1) & 1, &no_abort);
-            no_abort = 0;
-          }
+        if (kA2QRot) {
+          if (qldx0) mbar_wait(q_full, (qldx0 - 1) & 1, &no_abort);
+          no_abort = 0;
+          if (qldx1) mbar_wait(q_full + 1, (qldx1 - 1) & 1, &no_abort);
+          no_abort = 0;
+          if (qld[1]) mbar_wait(q_full_b, (qld[1] - 1) & 1, &no_abort);
+          no_abort = 0;
+        } else {
+          for (int t = 0; t < 2; ++t)
+            if (qld[t]) {
+              mbar_wait(q_full + t, (qld[t] - 1) & 1, &no_abort);
+              no_abort = 0;
+            }
+        }
       }
     } else if (kA2SplitProducer && warp == 2 && lane == 0) {
       // ------------------------------------------------------------ V producer
@@ -857,6 +911,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
       // std::integral_constant) and per-stage counters are two scalars, so nothing of it lives
       // in local memory.
       uint32_t it = 0, kvseq = 0, qc[2] = {0, 0}, pc[2] = {0, 0}, oc[2] = {0, 0};
+      uint32_t pi = 0, qcx0 = 0, qcx1 = 0;  // FPB_A2_QROT: items started, waits per Q_0 buffer
       int users0 = 0, users1 = 0;  // PVs still to be issued on the V tile of stage 0 / 1
       using T0 = std::integral_constant<int, 0>;
       using T1 = std::integral_constant<int, 1>;
@@ -872,6 +927,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         int pend[2] = {-1, -1};  // union sequence number of the block whose PV is due
         bool first[2] = {true, true}, qw[2] = {false, false};
         int s_left[2] = {n0, n1};  // S MMAs still to issue per tile; Q_t is free after the last
+        const int xs = pi & 1;     // FPB_A2_QROT: this item's Q_0 buffer
         auto issue_pv = [&](auto tt) -> bool {
           constexpr int t = decltype(tt)::value;
           const int q = pend[t], st = q & 1;
@@ -904,13 +960,18 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         auto issue_s = [&](auto tt, int st) -> bool {
           constexpr int t = decltype(tt)::value;
           if (!qw[t]) {
-            if (!A2_W(13, A2_MMA_WAIT(q_full + t, qc[t] & 1, abort))) return false;
-            ++qc[t];
+            if (kA2QRot && t == 0) {
+              if (!A2_W(13, A2_MMA_WAIT(q_full + xs, (xs ? qcx1 : qcx0) & 1, abort))) return false;
+              if (xs) ++qcx1; else ++qcx0;
+            } else {
+              if (!A2_W(13, A2_MMA_WAIT(kA2QRot ? q_full_b : q_full + t, qc[t] & 1, abort))) return false;
+              ++qc[t];
+            }
             qw[t] = true;
           }
           tc_fence_after();
           A2_EV(13, t);
-          const uint32_t qb_ = q_base + t * kA2Tile, kb_ = k_base + st * kA2Tile;
+          const uint32_t qb_ = q_base + (kA2QRot ? (t ? 2 : xs) : t) * kA2Tile, kb_ = k_base + st * kA2Tile;
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks) {
             const uint32_t off = (ks >> 2) * kA2Half + (ks & 3) * 32;
@@ -947,12 +1008,13 @@ __global__ void __launch_bounds__(kA2Threads, 1)
         if (pend[1] >= 0 && !issue_pv(T1{})) break;
         if (n0 > 0) {
           umma_commit(o_full);
-          if (!kA2EarlyQFree) umma_commit(q_empty);
+          if (!kA2EarlyQFree && !kA2QRot) umma_commit(q_empty);
         }
         if (n1 > 0) {
           umma_commit(o_full + 1);
           if (!kA2EarlyQFree) umma_commit(q_empty + 1);
         }
+        ++pi;
       }
       umma_commit(mma_done);
       volatile int no_abort = 0;
@@ -969,6 +1031,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
     const uint32_t t_o = tmem + 256 + t * 128 + lane_off;
     const float c = A.c;
     uint32_t it = 0, sc = 0, oc = 0, ep = 0, pw = 0;
+    uint32_t ps = 0;  // FPB_A2_QROT: items started (the issuer works on them)
     // a tile's per-row event: every thread's arrival, or (FPB_A2_WARP_ARRIVE) the warp's, once all
     // its lanes are past their fences
     auto row_arrive = [&](uint64_t* bar) {
@@ -990,10 +1053,23 @@ __global__ void __launch_bounds__(kA2Threads, 1)
       const Item2* fp = ring + slot;
       const int valid = fp->valid, h_t = fp->h[t], n = fp->n[t], diag_t = fp->diag[t], nfull_t = fp->nfull[t];
       const int start = fp->start, len = fp->len, bcoord = fp->bcoord, qbk = fp->qb, chunk = fp->chunk;
+      // FPB_A2_QROT: every softmax thread reports once per item the issuer works on that it is
+      // done with it (its epilogue staged rows in the item's Q_0 buffer)
+      const bool issued = valid == 1 && (fp->n[0] > 0 || fp->n[1] > 0);
+      uint8_t* const stage_base = kA2QRot ? sQ + (ps & 1) * kA2Tile : sStage;
+      auto item_end = [&]() {
+        if (kA2QRot && issued) {
+          mbar_arrive(stg_done + (ps & 1));
+          ++ps;
+        }
+      };
       mbar_arrive(item_empty + slot);
       ++it;
       if (valid == 0) break;
-      if (valid != 1 || h_t < 0) continue;
+      if (valid != 1 || h_t < 0) {
+        item_end();
+        continue;
+      }
       // rows this thread may write: inside the sequence and (chunked prefill) at or after q_off
       const int vr = min(kBlock, len - qbk * kBlock);
       const bool row_out = r < vr && qbk * kBlock + r >= A.P.q_off;
@@ -1008,6 +1084,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
           for (int i = 0; i < 16; ++i) dst[i] = make_uint4(0, 0, 0, 0);
         }
         if constexpr (kPeers) warp_rows_to_peers<T>(A, orow, zero_row);
+        item_end();
         continue;
       }
       float m_use = -INFINITY, l = 0.f;
@@ -1221,16 +1298,17 @@ __global__ void __launch_bounds__(kA2Threads, 1)
           if constexpr (kPeers) warp_rows_to_peers<T>(A, orow, row_out);  // the merged rows, sent on
         }
         A2_ADD(21, A2_CLK() - te0);
+        item_end();
         continue;
       }
       const float inv = 1.f / l;
-      if (kA2StageBytes > 0) {
+      if (kA2StageBytes > 0 || kA2QRot) {
         // lane = row; half h of the 32 rows goes through shared memory (piece q of a row at slot
         // q ^ (row & 7), conflict-free both ways), then out four rows per store instruction
         const uint64_t pol = l2_policy_evict_first();
         // tile t's warps use [t * half, (t + 1) * half) of the area (with P in shared memory:
         // of P_t, which its last PV has read: o_full_t is committed after it)
-        uint4* stg = reinterpret_cast<uint4*>(sStage + t * (kA2StageBytes / 2)) + quad * 256;
+        uint4* stg = reinterpret_cast<uint4*>(stage_base + t * (kA2PSmem ? kA2Tile : kA2Tile / 2)) + quad * 256;
         const unsigned vmask = __ballot_sync(0xffffffffu, row_out);
         const long long mine = reinterpret_cast<long long>(orow);
         long long rows[8];
@@ -1270,6 +1348,7 @@ __global__ void __launch_bounds__(kA2Threads, 1)
       }
       if constexpr (kPeers) warp_rows_to_peers<T>(A, orow, row_out);
       A2_ADD(21, A2_CLK() - te0);
+      item_end();
     }
   }
 
